@@ -1,0 +1,416 @@
+#!/usr/bin/env python
+"""Benchmark of mojodgl's B200 message-passing hot path (driver contract).
+
+Workload (the metric's multi-GPU config): a GraphSAGE-style
+aggregation on a synthetic 125M-edge power-law graph, N = 2.5M nodes,
+out-degrees lognormal(3.2, 1.3) capped at 20,000 and scaled to sum to exactly
+125,000,000 (floor + largest remainder), src-major edge order, destinations
+uniform, h = (N, 128) float32 ~ U(-1, 1); draws in that order from
+numpy.random.default_rng(3).  One step = one gSpMM copy_u_mean over all edges
+(``ops.copy_u_mean``), the config's first op; copy_u_max with arg-index output
+and copy_u_sum are timed beside it under "ops".
+
+Multi-GPU (torchrun, one rank per GPU): strong scaling of the same graph,
+destination rows partitioned by in-edge count, features owned in equal row
+blocks; a step is one NCCL all-gather of h (the halo) plus the local gSpMM.
+
+Prints one JSON line (rank 0).  ``--impl reference`` times the CPU
+restatement of the reference's Mojo kernels (oracle/, the reference itself
+cannot be built here) on the same workload and prints its line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "mojo-dgl_b200"))
+sys.path.insert(0, ROOT)
+
+CFG3 = dict(num_nodes=2_500_000, num_edges=125_000_000, dim=128, seed=3)
+METRIC = "gSpMM Gedge-feat/s"
+UNIT = "Gedge-feat/s"
+CPU_SAMPLE_EDGES = 1 << 23
+
+
+# ----------------------------------------------------------------- workload
+def make_cfg3(num_nodes, num_edges, dim, seed, with_h=True):
+    """Config 3's graph (and features) as numpy arrays, in the draw order of
+    the module docstring."""
+    rng = np.random.default_rng(seed)
+    w = np.minimum(rng.lognormal(3.2, 1.3, num_nodes), 20_000.0)
+    x = w * (num_edges / w.sum())
+    deg = np.floor(x).astype(np.int64)
+    short = num_edges - int(deg.sum())
+    if short > 0:
+        deg[np.argsort(-(x - deg), kind="stable")[:short]] += 1
+    u = np.repeat(np.arange(num_nodes, dtype=np.int64), deg)
+    v = rng.integers(0, num_nodes, num_edges, dtype=np.int64)
+    h = None
+    if with_h:
+        h = rng.random((num_nodes, dim), dtype=np.float32)
+        h *= 2.0
+        h -= 1.0
+    return u, v, h
+
+
+def algorithmic_bytes(num_rows, num_edges, dim, elem=4, arg=False):
+    """Gathered model: every edge's source row counted once per edge, plus
+    the int32 neighbour ids, the output rows and the int64 row pointers
+    (+ int64 arg indices for max/min)."""
+    b = num_edges * dim * elem + num_edges * 4 + num_rows * dim * elem + (num_rows + 1) * 8
+    if arg:
+        b += num_rows * dim * 8
+    return b
+
+
+# ------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples during the timed region (read-only queries)."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.FIELDS,
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[4:8]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------ CPU baselines
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_sample(u, v, h, num_nodes, sample_edges):
+    """A dst-row prefix of the graph holding ~sample_edges in-edges, as the
+    reference's in-CSR (stable by destination), for the oracle."""
+    rows = max(1, int(num_nodes * sample_edges / max(u.size, 1)))
+    sel = np.nonzero(v < rows)[0]
+    order = sel[np.argsort(v[sel], kind="stable")]
+    indeg = np.bincount(v[sel], minlength=rows).astype(np.int64)
+    indptr = np.zeros(rows + 1, dtype=np.int64)
+    np.cumsum(indeg, out=indptr[1:])
+    indices = np.ascontiguousarray(u[order], dtype=np.int64)
+    eid = np.arange(order.size, dtype=np.int64)
+    return rows, indptr, indices, eid, indeg
+
+
+def time_oracle(u, v, h, num_nodes, dim, sample_edges, repeats):
+    """The CPU restatement of the reference kernel (fp64, its 32-worker
+    split, every host thread OpenMP offers) on a bounded sample; returns
+    (Gedge-feat/s per repeat, threads, sample description)."""
+    threads = min(32, cpu_threads())
+    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    from oracle import oracle as orc
+
+    lib = orc.lib()
+    rows, indptr, indices, eid, indeg = cpu_sample(u, v, h, num_nodes, sample_edges)
+    h64 = np.ascontiguousarray(h, dtype=np.float64)  # the reference's f64() gate
+    out = np.empty((rows, dim), dtype=np.float64)
+    ne = int(indices.size)
+    rates = []
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        lib.mdgl_gspmm(indptr.ctypes.data, indices.ctypes.data, eid.ctypes.data, h64.ctypes.data,
+                       h64.ctypes.data, out.ctypes.data, rows, 5, dim, dim, dim, 3,
+                       indeg.ctypes.data)
+        dt = time.perf_counter() - t0
+        rates.append(ne * dim / dt / 1e9)
+    desc = ("copy_u_mean on the first {} destination rows of config 3 ({} in-edges, "
+            "{:.2%} of the graph), fp64, {} OpenMP threads over the reference's 32-worker "
+            "split".format(rows, ne, ne / max(u.size, 1), int(lib.oref_threads())))
+    return rates, int(lib.oref_threads()), desc
+
+
+# --------------------------------------------------------------- main paths
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), \
+        int(os.environ.get("LOCAL_RANK", 0))
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    c = CFG3
+    u, v, h = make_cfg3(**c)
+    for _ in range(args.warmup):
+        pass
+    rates, threads, desc = time_oracle(u, v, h, c["num_nodes"], c["dim"], CPU_SAMPLE_EDGES,
+                                       args.warmup + args.steps)
+    rates = rates[args.warmup:]
+    value = statistics.median(rates)
+    ms = c["num_edges"] * c["dim"] / (value * 1e9) * 1e3
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic",
+        "config": {"workload": "cfg3 copy_u_mean, N=2.5M, E=125M, D=128 (sampled on CPU)",
+                   "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference's Mojo library cannot be built in this image (no Mojo toolchain); "
+                "this arm times oracle/ported_ref.c, a C restatement of src/ported.mojo",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def load_traffic():
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import mojodgl as dgl
+    from mojodgl import ops
+    from mojodgl.partition import DeviceShard, DstShard, edge_balanced_ranges, owner_blocks
+
+    rank, world, local = dist_env()
+    if world > 1:
+        torch.cuda.set_device(local)
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    c = CFG3
+    n, e_total, d = c["num_nodes"], c["num_edges"], c["dim"]
+    u, v, h = make_cfg3(**c)
+
+    # -------- graph shard on this rank: dst rows balanced by in-edges
+    indeg = np.bincount(v, minlength=n)
+    bounds = edge_balanced_ranges(indeg, world)
+    lo, hi = int(bounds[rank]), int(bounds[rank + 1])
+    shard = DeviceShard(DstShard(u, v, lo, hi))
+    blk, owners = owner_blocks(n, world)
+    own_lo, own_hi = owners[rank]
+    h_dev = torch.from_numpy(h).to(dev)  # full features (kernel-only timing)
+    gathered = torch.empty((blk * world, d), dtype=torch.float32, device=dev)
+    my_block = torch.zeros((blk, d), dtype=torch.float32, device=dev)
+    my_block[: own_hi - own_lo] = h_dev[own_lo:own_hi]
+    out = torch.empty((hi - lo, d), dtype=torch.float32, device=dev)
+    ws = None
+    torch.cuda.synchronize()
+
+    def step():
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, my_block)
+            feat = gathered
+        else:
+            feat = h_dev
+        shard.copy_u(feat, "mean", out=out, workspace=ws)
+
+    def timed(fn, steps, warmup):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(steps):
+            fn()
+        s1.record()
+        torch.cuda.synchronize()
+        ms = s0.elapsed_time(s1) / steps
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    # the whole step (halo + local gSpMM): the headline value
+    with ClockSampler(local) as clocks:
+        ms_step = timed(step, args.steps, args.warmup)
+    # the gSpMM call alone (coords + main + fixup kernels) for the roofline
+    feat = h_dev
+    ms_kernel = timed(lambda: shard.copy_u(feat, "mean", out=out, workspace=ws), args.steps, 1)
+    value = e_total * d / (ms_step * 1e-3) / 1e9
+
+    # other ops of the config, device resident, this rank's shard
+    extra = {}
+    arg_u = torch.empty((hi - lo, d), dtype=torch.int64, device=dev)
+    for name, red, arg in (("copy_u_sum", "sum", None), ("copy_u_max+arg_u", "max", arg_u)):
+        ms_op = timed(lambda: shard.copy_u(feat, red, out=out, arg_u=arg), args.steps, 1)
+        extra[name] = {"ms": ms_op, "Gedge_feat_s": e_total * d / (ms_op * 1e-3) / 1e9 if world == 1
+                       else None,
+                       "achieved_GBps": algorithmic_bytes(hi - lo, shard.shard.num_edges, d,
+                                                          arg=arg is not None) / (ms_op * 1e-3) / 1e9}
+    del arg_u
+
+    # -------- e2e through the public API with host buffers
+    e2e = None
+    if world == 1:
+        g = dgl.graph((u, v), num_nodes=n)
+        g._device()  # the graph (its device CSR) is built once, like a user's
+        h_pin = torch.from_numpy(h).pin_memory()
+        for _ in range(2):
+            ops.copy_u_mean(g, h_pin)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            r = ops.copy_u_mean(g, h_pin)
+        torch.cuda.synchronize()
+        dt = (time.perf_counter() - t0) / args.steps
+        e2e = {"value": e_total * d / dt / 1e9, "unit": UNIT,
+               "h2d_bytes_per_step": int(h.nbytes), "d2h_bytes_per_step": int(r.numel() * 4),
+               "ms_per_step": dt * 1e3, "path": "ops.copy_u_mean(g, pinned CPU tensor)"}
+        del g, h_pin, r
+    else:
+        h_pin = torch.from_numpy(np.ascontiguousarray(h[own_lo:own_hi])).pin_memory()
+        out_pin = torch.empty((hi - lo, d), dtype=torch.float32).pin_memory()
+
+        def e2e_step():
+            my_block[: own_hi - own_lo].copy_(h_pin, non_blocking=True)
+            dist.all_gather_into_tensor(gathered, my_block)
+            shard.copy_u(gathered, "mean", out=out, workspace=ws)
+            out_pin.copy_(out, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+
+        for _ in range(2):
+            e2e_step()
+        dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            e2e_step()
+        dt = time.perf_counter() - t0
+        t = torch.tensor([dt / args.steps], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt = float(t.item())
+        e2e = {"value": e_total * d / dt / 1e9, "unit": UNIT,
+               "h2d_bytes_per_step": int(h.nbytes), "d2h_bytes_per_step": int(n * d * 4),
+               "ms_per_step": dt * 1e3,
+               "path": "per rank: pinned h block H2D, NCCL all-gather, gSpMM, output rows D2H"}
+
+    # -------- roofline of the dominant kernel (this rank's gSpMM)
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except (OSError, ValueError):
+        pass
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+    alg = algorithmic_bytes(hi - lo, shard.shard.num_edges, d)
+    achieved = alg / (ms_kernel * 1e-3) / 1e9
+    traffic = load_traffic().get("cfg3_copy_u_mean_world{}".format(world))
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "traffic": traffic,
+                "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
+                "kernel": "bgl_gspmm copy_u mean (k_spmm_coords + k_spmm + k_spmm_fixup)",
+                "algorithmic_bytes": alg, "kernel_ms": ms_kernel}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        rates, threads, desc = time_oracle(u, v, h, n, d, CPU_SAMPLE_EDGES, 3)
+        cpu = {"value": max(rates), "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": desc + " (best of 3)"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "cfg3 copy_u_mean (BASELINE config 3): N=2.5M, E=125M "
+                                   "lognormal out-degree, D=128 fp32",
+                       "num_nodes": n, "num_edges": e_total, "dim": d, "seed": c["seed"],
+                       "parallelism": "dst-row shards x{} + NCCL all-gather halo".format(world)
+                       if world > 1 else "single GPU",
+                       "l2": "inputs larger than L2 (h 1.28 GB, indices 0.5 GB)"},
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": 3 * args.steps,
+            "clocks": clocks.summary(), "ops": extra,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

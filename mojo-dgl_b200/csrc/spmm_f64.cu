@@ -1,0 +1,51 @@
+// gSpMM kernel instantiations for double (one translation unit per element type
+// so the double and the other element type's kernels compile in parallel).
+#include "spmm_impl.cuh"
+
+namespace bgl {
+namespace {
+
+template <typename T, int OP, int RED, int V, int J>
+int launch_one(const SpmmArgs<T> &a, cudaStream_t s) {
+    int64_t threads = a.num_chunks * a.ts;
+    int grid = (int)((threads + 255) / 256);
+    if (grid < 1) grid = 1;
+    k_spmm<T, OP, RED, V, J><<<grid, 256, 0, s>>>(a);
+    BGL_LAUNCH_CHECK();
+    k_spmm_fixup<T, RED, V, J><<<grid, 256, 0, s>>>(a);
+    BGL_LAUNCH_CHECK();
+    return BGL_OK;
+}
+
+template <typename T, int OP, int V, int J>
+int by_reduce(const SpmmArgs<T> &a, int red, cudaStream_t s) {
+    switch (red) {
+    case BGL_RED_SUM:
+    case BGL_RED_MEAN: return launch_one<T, OP, BGL_RED_SUM, V, J>(a, s);
+    case BGL_RED_MAX: return launch_one<T, OP, BGL_RED_MAX, V, J>(a, s);
+    case BGL_RED_MIN: return launch_one<T, OP, BGL_RED_MIN, V, J>(a, s);
+    }
+    return fail(BGL_E_INVALID, "gspmm: reduce code %d", red);
+}
+
+}  // namespace
+
+template <typename T, int V, int J>
+int launch_spmm_vj(const SpmmArgs<T> &a, int op, int red, cudaStream_t s) {
+    switch (op) {
+    case BGL_OP_ADD: return by_reduce<T, BGL_OP_ADD, V, J>(a, red, s);
+    case BGL_OP_SUB: return by_reduce<T, BGL_OP_SUB, V, J>(a, red, s);
+    case BGL_OP_MUL: return by_reduce<T, BGL_OP_MUL, V, J>(a, red, s);
+    case BGL_OP_DIV: return by_reduce<T, BGL_OP_DIV, V, J>(a, red, s);
+    case BGL_OP_COPY_LHS: return by_reduce<T, BGL_OP_COPY_LHS, V, J>(a, red, s);
+    case BGL_OP_COPY_RHS: return by_reduce<T, BGL_OP_COPY_RHS, V, J>(a, red, s);
+    }
+    return fail(BGL_E_INVALID, "gspmm: op code %d", op);
+}
+
+template int launch_spmm_vj<double, 1, 1>(const SpmmArgs<double> &, int, int, cudaStream_t);
+template int launch_spmm_vj<double, 1, 4>(const SpmmArgs<double> &, int, int, cudaStream_t);
+template int launch_spmm_vj<double, 2, 1>(const SpmmArgs<double> &, int, int, cudaStream_t);
+template int launch_spmm_vj<double, 2, 4>(const SpmmArgs<double> &, int, int, cudaStream_t);
+
+}  // namespace bgl

@@ -1,0 +1,299 @@
+// gSpMM engine (replaces src/ported.mojo:352-548, _gspmm and its dispatch).
+//
+// Work split: merge-path over the (row ends, edges) sequence of the CSR.  The
+// N + E items are cut into equal chunks, one per team of lanes; a boundary
+// that falls inside a row no longer than `split_min` edges is moved back to
+// that row's start, so only rows longer than a chunk are ever split.  That
+// gives every team the same amount of work whatever the degree distribution
+// (power-law hubs included) while keeping the reference's arithmetic for all
+// ordinary rows: each lane owns V consecutive output columns and folds the
+// row's messages in CSR order, one rounding per message and one per add,
+// exactly as the reference's per-column loop does (src/ported.mojo:392-422).
+//
+// A split row leaves one piece per chunk it touches in the workspace; the
+// fixup kernel folds the pieces in CSR order (a sum of partial sums, so the
+// rounding differs from the sequential loop only for those rows; max/min and
+// their arg indices stay exact because a later piece replaces the running
+// winner only on a strict improvement, the reference's rule at
+// src/ported.mojo:106-109).
+#pragma once
+
+#include "common.cuh"
+
+namespace bgl {
+
+struct Coord {
+    int64_t x;  // rows finished
+    int64_t y;  // edges consumed
+};
+
+template <typename T>
+struct SpmmArgs {
+    const int64_t *indptr;
+    const int32_t *indices;
+    const int32_t *eid;
+    const int64_t *deg;
+    int64_t num_rows;
+    int64_t num_edges;
+    Operand<T> lhs, rhs;
+    T *out;
+    int64_t dout;
+    int64_t *arg_u;
+    int64_t *arg_e;
+    bool mean;
+    bool zero_inf;
+    int ts;  // lanes per team (power of two <= 32)
+    int64_t num_chunks;
+    const Coord *coords;  // num_chunks + 1 boundaries
+    T *head_val;
+    T *tail_val;
+    int32_t *head_pos;
+    int32_t *tail_pos;
+    int64_t *head_row;
+    int64_t *tail_row;
+};
+
+// Merge-path diagonal search (Merrill & Garland, "Merge-based parallel sparse
+// matrix-vector multiplication", SC'16), with the small-row snap.
+__device__ __forceinline__ Coord merge_coord(const int64_t *__restrict__ indptr, int64_t n,
+                                             int64_t e, int64_t diag, int64_t split_min) {
+    int64_t lo = diag - e > 0 ? diag - e : 0;
+    int64_t hi = diag < n ? diag : n;
+    while (lo < hi) {
+        int64_t mid = (lo + hi) >> 1;
+        if (indptr[mid + 1] <= diag - mid - 1)
+            lo = mid + 1;
+        else
+            hi = mid;
+    }
+    Coord c{lo, diag - lo};
+    if (c.x < n) {
+        int64_t rs = indptr[c.x];
+        if (c.y > rs && indptr[c.x + 1] - rs <= split_min) c.y = rs;
+    }
+    return c;
+}
+
+static __global__ void k_spmm_coords(const int64_t *__restrict__ indptr, int64_t n, int64_t e,
+                              int64_t items, int64_t split_min, int64_t num_chunks,
+                              Coord *__restrict__ coords) {
+    for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c <= num_chunks;
+         c += (int64_t)gridDim.x * blockDim.x) {
+        int64_t diag = c * items;
+        if (diag > n + e) diag = n + e;
+        coords[c] = merge_coord(indptr, n, e, diag, split_min);
+    }
+}
+
+template <int RED, typename T>
+__device__ __forceinline__ T identity() {
+    if (RED == BGL_RED_MAX) return Arith<T>::ninf();
+    if (RED == BGL_RED_MIN) return Arith<T>::pinf();
+    return T(0);
+}
+
+// Folds message m (at CSR position p) into the running value.
+template <int RED, typename T>
+__device__ __forceinline__ void fold(T &acc, int32_t &pos, T m, int32_t p) {
+    if (RED == BGL_RED_MAX) {
+        if (m > acc) { acc = m; pos = p; }
+    } else if (RED == BGL_RED_MIN) {
+        if (m < acc) { acc = m; pos = p; }
+    } else {
+        acc = Arith<T>::add(acc, m);
+    }
+}
+
+// Writes one finished row: the mean divide, the inf->0 post-pass and the arg
+// indices are all applied here, so the row is written once.
+template <typename T, int RED, int V, int J>
+__device__ __forceinline__ void emit_row(const SpmmArgs<T> &a, int64_t row, int64_t cb, int t,
+                                         int64_t cvn, const T (&acc)[J][V],
+                                         const int32_t (&pos)[J][V]) {
+    T scale = T(1);
+    if (a.mean) {
+        int64_t dg = a.deg ? a.deg[row] : a.indptr[row + 1] - a.indptr[row];
+        scale = dg < 1 ? T(1) : T(dg);
+    }
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        int64_t cv = cb + t + (int64_t)j * a.ts;
+        if (cv >= cvn) continue;
+        int64_t off = row * a.dout + cv * V;
+        T o[V];
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+            T v = acc[j][i];
+            if (a.mean) v = Arith<T>::div(v, scale);
+            if (a.zero_inf && isinf(v)) v = T(0);
+            o[i] = v;
+        }
+        store_vec<T, V>(a.out + off, o);
+        if (RED == BGL_RED_MAX || RED == BGL_RED_MIN) {
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+                int32_t p = pos[j][i];
+                if (a.arg_u) a.arg_u[off + i] = p < 0 ? -1 : (int64_t)a.indices[p];
+                if (a.arg_e) a.arg_e[off + i] = p < 0 ? -1 : (a.eid ? (int64_t)a.eid[p] : (int64_t)p);
+            }
+        }
+    }
+}
+
+template <typename T, int RED, int V, int J>
+__device__ __forceinline__ void store_piece(const SpmmArgs<T> &a, T *val, int32_t *pz,
+                                            int64_t chunk, int64_t cb, int t, int64_t cvn,
+                                            const T (&acc)[J][V], const int32_t (&pos)[J][V]) {
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        int64_t cv = cb + t + (int64_t)j * a.ts;
+        if (cv >= cvn) continue;
+        int64_t off = chunk * a.dout + cv * V;
+        store_vec<T, V>(val + off, acc[j]);
+        if (RED == BGL_RED_MAX || RED == BGL_RED_MIN) {
+#pragma unroll
+            for (int i = 0; i < V; ++i) pz[off + i] = pos[j][i];
+        }
+    }
+}
+
+template <typename T, int OP, int RED, int V, int J>
+__global__ void __launch_bounds__(256) k_spmm(const SpmmArgs<T> a) {
+    constexpr int UN = (J == 1) ? 8 : 2;  // edges in flight per lane
+    constexpr bool NEED_L = OP != BGL_OP_COPY_RHS;
+    constexpr bool NEED_R = OP != BGL_OP_COPY_LHS;
+    const int ts = a.ts;
+    const int t = threadIdx.x & (ts - 1);
+    const int64_t chunk = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) / ts;
+    if (chunk >= a.num_chunks) return;
+    const Coord c0 = a.coords[chunk];
+    const Coord c1 = a.coords[chunk + 1];
+    const int64_t cvn = a.dout / V;
+    const int64_t *__restrict__ indptr = a.indptr;
+
+    int64_t head_row = -1, tail_row = -1;
+    for (int64_t cb = 0; cb < cvn; cb += (int64_t)ts * J) {
+        int64_t x = c0.x, y = c0.y;
+        while (x < c1.x || (x == c1.x && y < c1.y)) {
+            const int64_t rs = indptr[x];
+            const int64_t re = indptr[x + 1];
+            const int64_t eb = y;
+            const int64_t ee = (x < c1.x) ? re : c1.y;
+            T acc[J][V];
+            int32_t pos[J][V];
+#pragma unroll
+            for (int j = 0; j < J; ++j)
+#pragma unroll
+                for (int i = 0; i < V; ++i) {
+                    acc[j][i] = identity<RED, T>();
+                    pos[j][i] = -1;
+                }
+            for (int64_t e = eb; e < ee; e += UN) {
+                const int n = (ee - e) < UN ? (int)(ee - e) : UN;
+                int32_t src[UN], edg[UN];
+#pragma unroll
+                for (int u = 0; u < UN; ++u) {
+                    if (u < n) {
+                        if (NEED_L) src[u] = __ldg(a.indices + e + u);
+                        if (NEED_R) edg[u] = a.eid ? __ldg(a.eid + e + u) : (int32_t)(e + u);
+                    }
+                }
+                T lv[UN][J][V], rv[UN][J][V];
+#pragma unroll
+                for (int u = 0; u < UN; ++u) {
+                    if (u < n) {
+#pragma unroll
+                        for (int j = 0; j < J; ++j) {
+                            int64_t cv = cb + t + (int64_t)j * ts;
+                            if (cv < cvn) {
+                                if (NEED_L) load_cols<T, V>(a.lhs, src[u], cv * V, lv[u][j]);
+                                if (NEED_R) load_cols<T, V>(a.rhs, edg[u], cv * V, rv[u][j]);
+                            }
+                        }
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < UN; ++u) {
+                    if (u < n) {
+#pragma unroll
+                        for (int j = 0; j < J; ++j) {
+#pragma unroll
+                            for (int i = 0; i < V; ++i) {
+                                T m = message<OP, T>(NEED_L ? lv[u][j][i] : T(0),
+                                                     NEED_R ? rv[u][j][i] : T(0));
+                                fold<RED, T>(acc[j][i], pos[j][i], m, (int32_t)(e + u));
+                            }
+                        }
+                    }
+                }
+            }
+            if (x < c1.x) {
+                if (eb == rs) {
+                    emit_row<T, RED, V, J>(a, x, cb, t, cvn, acc, pos);
+                } else {
+                    store_piece<T, RED, V, J>(a, a.head_val, a.head_pos, chunk, cb, t, cvn, acc, pos);
+                    head_row = x;
+                }
+                y = re;
+                ++x;
+            } else {
+                store_piece<T, RED, V, J>(a, a.tail_val, a.tail_pos, chunk, cb, t, cvn, acc, pos);
+                tail_row = x;
+                break;
+            }
+        }
+    }
+    if (t == 0) {
+        a.head_row[chunk] = head_row;
+        a.tail_row[chunk] = tail_row;
+    }
+}
+
+// Folds the pieces of every split row in CSR order and writes the row.
+template <typename T, int RED, int V, int J>
+__global__ void __launch_bounds__(256) k_spmm_fixup(const SpmmArgs<T> a) {
+    const int ts = a.ts;
+    const int t = threadIdx.x & (ts - 1);
+    const int64_t chunk = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) / ts;
+    if (chunk >= a.num_chunks) return;
+    const int64_t row = a.head_row[chunk];
+    if (row < 0) return;
+    int64_t first = chunk;
+    while (first > 0 && a.tail_row[first - 1] == row) --first;
+    const int64_t cvn = a.dout / V;
+    for (int64_t cb = 0; cb < cvn; cb += (int64_t)ts * J) {
+        T acc[J][V];
+        int32_t pos[J][V];
+#pragma unroll
+        for (int j = 0; j < J; ++j)
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+                acc[j][i] = identity<RED, T>();
+                pos[j][i] = -1;
+            }
+        for (int64_t q = first; q <= chunk; ++q) {
+            const T *val = (q == chunk) ? a.head_val : a.tail_val;
+            const int32_t *pz = (q == chunk) ? a.head_pos : a.tail_pos;
+#pragma unroll
+            for (int j = 0; j < J; ++j) {
+                int64_t cv = cb + t + (int64_t)j * ts;
+                if (cv >= cvn) continue;
+                int64_t off = q * a.dout + cv * V;
+                T pv[V];
+                load_vec<T, V>(val + off, pv);
+#pragma unroll
+                for (int i = 0; i < V; ++i) {
+                    int32_t pp = (RED == BGL_RED_MAX || RED == BGL_RED_MIN) ? pz[off + i] : 0;
+                    fold<RED, T>(acc[j][i], pos[j][i], pv[i], pp);
+                }
+            }
+        }
+        emit_row<T, RED, V, J>(a, row, cb, t, cvn, acc, pos);
+    }
+}
+
+// Launches main + fixup for one (T, V, J) with runtime op/reduce dispatch.
+template <typename T, int V, int J>
+int launch_spmm_vj(const SpmmArgs<T> &a, int op, int red, cudaStream_t s);
+
+}  // namespace bgl
