@@ -243,7 +243,8 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
-    c = CFG3
+    c = dict(CFG3)
+    c["num_edges"] = int(round(c["num_edges"] * args.scale))
     n, e_total, d = c["num_nodes"], c["num_edges"], c["dim"]
     u, v, h = make_cfg3(**c)
 
@@ -300,7 +301,8 @@ def run_ours(args):
     # other ops of the config, device resident, this rank's shard
     extra = {}
     arg_u = torch.empty((hi - lo, d), dtype=torch.int64, device=dev)
-    for name, red, arg in (("copy_u_sum", "sum", None), ("copy_u_max+arg_u", "max", arg_u)):
+    for name, red, arg in (() if args.no_extra else
+                           (("copy_u_sum", "sum", None), ("copy_u_max+arg_u", "max", arg_u))):
         ms_op = timed(lambda: shard.copy_u(feat, red, out=out, arg_u=arg), args.steps, 1)
         extra[name] = {"ms": ms_op, "Gedge_feat_s": e_total * d / (ms_op * 1e-3) / 1e9 if world == 1
                        else None,
@@ -310,7 +312,9 @@ def run_ours(args):
 
     # -------- e2e through the public API with host buffers
     e2e = None
-    if world == 1:
+    if args.no_e2e:
+        pass
+    elif world == 1:
         g = dgl.graph((u, v), num_nodes=n)
         g._device()  # the graph (its device CSR) is built once, like a user's
         h_pin = torch.from_numpy(h).pin_memory()
@@ -381,7 +385,9 @@ def run_ours(args):
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": "cfg3 copy_u_mean (BASELINE config 3): N=2.5M, E=125M "
-                                   "lognormal out-degree, D=128 fp32",
+                                   "lognormal out-degree, D=128 fp32" if args.scale == 1.0 else
+                                   "cfg3 copy_u_mean with edges scaled by {} (profiling case)"
+                                   .format(args.scale),
                        "num_nodes": n, "num_edges": e_total, "dim": d, "seed": c["seed"],
                        "parallelism": "dst-row shards x{} + NCCL all-gather halo".format(world)
                        if world > 1 else "single GPU",
@@ -404,6 +410,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
+    ap.add_argument("--no-extra", action="store_true", help="skip the other ops of the config")
+    ap.add_argument("--scale", type=float, default=1.0,
+                    help="scale the edge count (a smaller case for profiling; nodes unchanged)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -66,7 +66,9 @@ const char *bgl_last_error(void);
 /* ABI revision of this header. */
 int bgl_abi_version(void);
 /* Tuning knobs for tests and benchmarks: "spmm_min_items" (merge-path chunk
- * floor), "spmm_max_chunks" (cap on merge-path chunks; 0 = automatic).
+ * floor), "spmm_max_chunks" (cap on merge-path chunks; 0 = automatic),
+ * "spmm_split_min" (rows with at most this many edges are never split across
+ * chunks; default 512).
  * Returns BGL_OK or BGL_E_INVALID for an unknown name. */
 int bgl_set_param(const char *name, int64_t value);
 

@@ -57,6 +57,11 @@ int bgl_set_param(const char *name, int64_t value) {
         bgl::params().spmm_max_chunks = value;
         return BGL_OK;
     }
+    if (std::strcmp(name, "spmm_split_min") == 0) {
+        if (value < 0) return bgl::fail(BGL_E_INVALID, "spmm_split_min must be >= 0");
+        bgl::params().spmm_split_min = value;
+        return BGL_OK;
+    }
     return bgl::fail(BGL_E_INVALID, "bgl_set_param: unknown parameter '%s'", name);
 }
 

@@ -33,8 +33,9 @@ int num_sms();  // SMs of the current device (cached per device)
 
 // Tuning parameters settable through bgl_set_param.
 struct Params {
-    int64_t spmm_min_items = 32;
-    int64_t spmm_max_chunks = 0;
+    int64_t spmm_min_items = 32;   // merge-path chunk floor (items = rows + edges)
+    int64_t spmm_max_chunks = 0;   // cap on chunks, 0 = automatic
+    int64_t spmm_split_min = 512;  // rows with at most this many edges are never split
 };
 Params &params();
 
@@ -111,6 +112,25 @@ __device__ __forceinline__ void load_vec(const T *p, T (&r)[V]) {
     for (int i = 0; i < V; ++i) r[i] = s[i];
 }
 
+// Read-only vector load that does not allocate in L1: gathered feature rows
+// are touched once per edge and essentially never hit L1.
+__device__ __forceinline__ void ld_stream(const float *p, float (&r)[4]) {
+    asm("ld.global.nc.L1::no_allocate.v4.f32 {%0, %1, %2, %3}, [%4];"
+        : "=f"(r[0]), "=f"(r[1]), "=f"(r[2]), "=f"(r[3]) : "l"(p));
+}
+__device__ __forceinline__ void ld_stream(const float *p, float (&r)[2]) {
+    asm("ld.global.nc.L1::no_allocate.v2.f32 {%0, %1}, [%2];" : "=f"(r[0]), "=f"(r[1]) : "l"(p));
+}
+__device__ __forceinline__ void ld_stream(const float *p, float (&r)[1]) {
+    asm("ld.global.nc.L1::no_allocate.f32 %0, [%1];" : "=f"(r[0]) : "l"(p));
+}
+__device__ __forceinline__ void ld_stream(const double *p, double (&r)[2]) {
+    asm("ld.global.nc.L1::no_allocate.v2.f64 {%0, %1}, [%2];" : "=d"(r[0]), "=d"(r[1]) : "l"(p));
+}
+__device__ __forceinline__ void ld_stream(const double *p, double (&r)[1]) {
+    asm("ld.global.nc.L1::no_allocate.f64 %0, [%1];" : "=d"(r[0]) : "l"(p));
+}
+
 template <typename T, int V>
 __device__ __forceinline__ void store_vec(T *p, const T (&r)[V]) {
     using VT = typename VecT<T, V>::type;
@@ -138,7 +158,7 @@ __device__ __forceinline__ void load_cols(const Operand<T> &o, int64_t row, int6
                                           T (&r)[V]) {
     const T *base = o.ptr + row * o.width;
     if (o.full) {
-        load_vec<T, V>(base + k0, r);
+        ld_stream(base + k0, r);
     } else if (o.uniform) {
         T x = __ldg(base + (k0 / o.div) % o.width);
 #pragma unroll

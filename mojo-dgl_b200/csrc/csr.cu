@@ -118,7 +118,7 @@ int bgl_csr_build(const int64_t *key, const int64_t *other, int64_t num_edges, i
         return fail(BGL_E_INVALID, "bgl_csr_build: negative size");
     if (num_edges >= (int64_t(1) << 31) || num_nodes >= (int64_t(1) << 31))
         return fail(BGL_E_UNSUPPORTED, "bgl_csr_build: more than 2^31-1 nodes or edges");
-    if (!indptr || !deg || !order || !indices || (num_edges && (!key || !other)))
+    if (!indptr || (num_nodes && !deg) || (num_edges && (!key || !other || !order || !indices)))
         return fail(BGL_E_INVALID, "bgl_csr_build: null pointer");
     if (workspace_bytes < bgl_csr_build_workspace_size(num_edges, num_nodes))
         return fail(BGL_E_WORKSPACE, "bgl_csr_build: workspace too small");

@@ -38,7 +38,9 @@ static SpmmPlan spmm_plan(int64_t n, int64_t e, int64_t dout, int dtype, int red
     if (p.num_chunks < 1) p.num_chunks = 1;
     p.items = (total + p.num_chunks - 1) / p.num_chunks;
     if (p.items < 1) p.items = 1;
-    p.split_min = p.items;
+    // a row is split only when it is longer than both a chunk and the
+    // split floor, so every ordinary row keeps the sequential CSR-order sum
+    p.split_min = p.items > params().spmm_split_min ? p.items : params().spmm_split_min;
     return p;
 }
 

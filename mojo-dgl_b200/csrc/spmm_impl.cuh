@@ -157,30 +157,77 @@ __device__ __forceinline__ void store_piece(const SpmmArgs<T> &a, T *val, int32_
     }
 }
 
+// Edges a lane keeps in flight: about eight vector loads per lane whatever
+// the row width, halved when both operands are gathered.
+// Measured on config 3 (125M edges, 128 fp32 columns): 4 edges in flight per
+// lane with 4 resident 256-thread blocks per SM (64 registers) ran copy_u sum
+// in 10.0 ms and max in 14.9 ms; 8 edges with 3 blocks: 10.0 / 22.2 ms; 8 with
+// 2 blocks: 11.2 / 31.7 ms -- occupancy beats per-lane depth once the walk
+// streams across row ends.
+#ifndef BGL_SPMM_UN
+#define BGL_SPMM_UN 4  // edges in flight per lane for rows of <= 32 vectors
+#endif
+#ifndef BGL_SPMM_MINB
+#define BGL_SPMM_MINB 4  // resident 256-thread blocks per SM the registers must allow
+#endif
+template <int OP, int J>
+struct InFlight {
+    static constexpr int both = (OP != BGL_OP_COPY_LHS && OP != BGL_OP_COPY_RHS) ? 2 : 1;
+    static constexpr int value = J == 1 ? BGL_SPMM_UN : (2 / both > 0 ? 2 / both : 1);
+};
+
+// The main pass.  A team walks its chunk's edge range [c0.y, c1.y) in full
+// groups of UN edges regardless of where rows end -- a group can close one
+// row and open the next -- so each lane always has UN row loads in flight,
+// and the next group's neighbour ids are fetched while the current group's
+// rows are still arriving.  Row ends are handled as the group is folded, in
+// CSR order, so the arithmetic is exactly the per-row sequential fold.
 template <typename T, int OP, int RED, int V, int J>
-__global__ void __launch_bounds__(256) k_spmm(const SpmmArgs<T> a) {
-    constexpr int UN = (J == 1) ? 8 : 2;  // edges in flight per lane
+__global__ void __launch_bounds__(256, (J == 1 ? BGL_SPMM_MINB : 2)) k_spmm(const SpmmArgs<T> a) {
+    constexpr int UN = InFlight<OP, J>::value;
     constexpr bool NEED_L = OP != BGL_OP_COPY_RHS;
     constexpr bool NEED_R = OP != BGL_OP_COPY_LHS;
     const int ts = a.ts;
     const int t = threadIdx.x & (ts - 1);
     const int64_t chunk = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) / ts;
     if (chunk >= a.num_chunks) return;
-    const Coord c0 = a.coords[chunk];
-    const Coord c1 = a.coords[chunk + 1];
-    const int64_t cvn = a.dout / V;
+    // rows and edges are below 2^31 (checked by the host), so the walk
+    // bookkeeping stays in 32-bit registers
+    const int32_t x0 = (int32_t)a.coords[chunk].x, y0 = (int32_t)a.coords[chunk].y;
+    const int32_t x1 = (int32_t)a.coords[chunk + 1].x, ye = (int32_t)a.coords[chunk + 1].y;
+    const int32_t nrows = (int32_t)a.num_rows;
+    const int32_t cvn = (int32_t)(a.dout / V);
     const int64_t *__restrict__ indptr = a.indptr;
 
-    int64_t head_row = -1, tail_row = -1;
-    for (int64_t cb = 0; cb < cvn; cb += (int64_t)ts * J) {
-        int64_t x = c0.x, y = c0.y;
-        while (x < c1.x || (x == c1.x && y < c1.y)) {
-            const int64_t rs = indptr[x];
-            const int64_t re = indptr[x + 1];
-            const int64_t eb = y;
-            const int64_t ee = (x < c1.x) ? re : c1.y;
-            T acc[J][V];
-            int32_t pos[J][V];
+    int32_t head_row = -1, tail_row = -1;
+    for (int32_t cb = 0; cb < cvn; cb += ts * J) {
+        int32_t x = x0;
+        if (x >= nrows) break;  // an empty trailing chunk
+        int32_t rs = (int32_t)indptr[x];
+        int32_t re = (x < x1) ? (int32_t)indptr[x + 1] : ye;
+        int32_t row_begin = y0;  // first edge of the current row in this chunk
+        T acc[J][V];
+        int32_t pos[J][V];
+#pragma unroll
+        for (int j = 0; j < J; ++j)
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+                acc[j][i] = identity<RED, T>();
+                pos[j][i] = -1;
+            }
+        // closes row x (emitted, or stored as a head piece if it began in an
+        // earlier chunk) and opens row x + 1
+        auto close_row = [&]() {
+            if (row_begin == rs) {
+                emit_row<T, RED, V, J>(a, x, cb, t, cvn, acc, pos);
+            } else {
+                store_piece<T, RED, V, J>(a, a.head_val, a.head_pos, chunk, cb, t, cvn, acc, pos);
+                head_row = x;
+            }
+            row_begin = re;
+            rs = re;
+            ++x;
+            re = (x < x1) ? (int32_t)indptr[x + 1] : ye;
 #pragma unroll
             for (int j = 0; j < J; ++j)
 #pragma unroll
@@ -188,59 +235,63 @@ __global__ void __launch_bounds__(256) k_spmm(const SpmmArgs<T> a) {
                     acc[j][i] = identity<RED, T>();
                     pos[j][i] = -1;
                 }
-            for (int64_t e = eb; e < ee; e += UN) {
-                const int n = (ee - e) < UN ? (int)(ee - e) : UN;
-                int32_t src[UN], edg[UN];
+        };
+
+        int32_t src[UN], edg[UN];
+        auto fetch_ids = [&](int32_t e0, int32_t(&s)[UN], int32_t(&d)[UN]) {
 #pragma unroll
-                for (int u = 0; u < UN; ++u) {
-                    if (u < n) {
-                        if (NEED_L) src[u] = __ldg(a.indices + e + u);
-                        if (NEED_R) edg[u] = a.eid ? __ldg(a.eid + e + u) : (int32_t)(e + u);
-                    }
+            for (int u = 0; u < UN; ++u) {
+                if (e0 + u < ye) {
+                    if (NEED_L) s[u] = __ldg(a.indices + e0 + u);
+                    if (NEED_R) d[u] = a.eid ? __ldg(a.eid + e0 + u) : e0 + u;
                 }
-                T lv[UN][J][V], rv[UN][J][V];
+            }
+        };
+        fetch_ids(y0, src, edg);
+        for (int32_t e0 = y0; e0 < ye; e0 += UN) {
+            const int n = (ye - e0) < UN ? (ye - e0) : UN;
+            T lv[UN][J][V], rv[UN][J][V];
 #pragma unroll
-                for (int u = 0; u < UN; ++u) {
-                    if (u < n) {
+            for (int u = 0; u < UN; ++u) {
+                if (u < n) {
 #pragma unroll
-                        for (int j = 0; j < J; ++j) {
-                            int64_t cv = cb + t + (int64_t)j * ts;
-                            if (cv < cvn) {
-                                if (NEED_L) load_cols<T, V>(a.lhs, src[u], cv * V, lv[u][j]);
-                                if (NEED_R) load_cols<T, V>(a.rhs, edg[u], cv * V, rv[u][j]);
-                            }
-                        }
-                    }
-                }
-#pragma unroll
-                for (int u = 0; u < UN; ++u) {
-                    if (u < n) {
-#pragma unroll
-                        for (int j = 0; j < J; ++j) {
-#pragma unroll
-                            for (int i = 0; i < V; ++i) {
-                                T m = message<OP, T>(NEED_L ? lv[u][j][i] : T(0),
-                                                     NEED_R ? rv[u][j][i] : T(0));
-                                fold<RED, T>(acc[j][i], pos[j][i], m, (int32_t)(e + u));
-                            }
+                    for (int j = 0; j < J; ++j) {
+                        const int32_t cv = cb + t + j * ts;
+                        if (cv < cvn) {
+                            if (NEED_L) load_cols<T, V>(a.lhs, src[u], (int64_t)cv * V, lv[u][j]);
+                            if (NEED_R) load_cols<T, V>(a.rhs, edg[u], (int64_t)cv * V, rv[u][j]);
                         }
                     }
                 }
             }
-            if (x < c1.x) {
-                if (eb == rs) {
-                    emit_row<T, RED, V, J>(a, x, cb, t, cvn, acc, pos);
-                } else {
-                    store_piece<T, RED, V, J>(a, a.head_val, a.head_pos, chunk, cb, t, cvn, acc, pos);
-                    head_row = x;
+            int32_t nsrc[UN], nedg[UN];
+            fetch_ids(e0 + UN, nsrc, nedg);
+#pragma unroll
+            for (int u = 0; u < UN; ++u) {
+                if (u < n) {
+                    const int32_t e = e0 + u;
+                    while (e >= re) close_row();
+#pragma unroll
+                    for (int j = 0; j < J; ++j)
+#pragma unroll
+                        for (int i = 0; i < V; ++i) {
+                            T m = message<OP, T>(NEED_L ? lv[u][j][i] : T(0),
+                                                 NEED_R ? rv[u][j][i] : T(0));
+                            fold<RED, T>(acc[j][i], pos[j][i], m, e);
+                        }
                 }
-                y = re;
-                ++x;
-            } else {
-                store_piece<T, RED, V, J>(a, a.tail_val, a.tail_pos, chunk, cb, t, cvn, acc, pos);
-                tail_row = x;
-                break;
             }
+#pragma unroll
+            for (int u = 0; u < UN; ++u) {
+                src[u] = nsrc[u];
+                edg[u] = nedg[u];
+            }
+        }
+        while (x < x1) close_row();  // rows ending at the chunk end, empty rows
+        if (x < nrows && ye > row_begin) {
+            // row x continues into the next chunk: its first (or middle) piece
+            store_piece<T, RED, V, J>(a, a.tail_val, a.tail_pos, chunk, cb, t, cvn, acc, pos);
+            tail_row = x;
         }
     }
     if (t == 0) {

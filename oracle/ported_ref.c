@@ -149,8 +149,11 @@ static void gsddmm_range(const i64 *uids, const i64 *vids, const f64 *lhs, const
             dst[e] = acc;
             continue;
         }
-        for (i64 d = 0; d < dout; ++d)
-            dst[e * dout + d] = message((int)op, lhs[li + d], rhs[ri + d]);
+        for (i64 d = 0; d < dout; ++d) {
+            f64 x = op == OP_COPY_RHS ? 0.0 : lhs[li + d];
+            f64 y = op == OP_COPY_LHS ? 0.0 : rhs[ri + d];
+            dst[e * dout + d] = message((int)op, x, y);
+        }
     }
 }
 
@@ -183,7 +186,13 @@ static void gspmm_range(const i64 *indptr, const i64 *indices, const i64 *eid, c
             f64 acc = seed_of(kred);
             i64 best = -1;
             for (i64 i = start; i < stop; ++i) {
-                f64 m = message(op, lhs[indices[i] * dl + k], rhs[eid[i] * dr + k]);
+                /* the operand a copy op does not use is never read: with
+                 * copy_lhs the reference passes rhs = lhs (spmm.py:64-66) and
+                 * eid can exceed its row count, a load its specialised
+                 * kernel drops at compile time */
+                f64 x = op == OP_COPY_RHS ? 0.0 : lhs[indices[i] * dl + k];
+                f64 y = op == OP_COPY_LHS ? 0.0 : rhs[eid[i] * dr + k];
+                f64 m = message(op, x, y);
                 if (kred == RED_MAX) {
                     if (m > acc) best = i;
                     acc = fmax_ref(acc, m);

@@ -43,9 +43,11 @@ def small_chunks():
     """Force merge-path chunks of ~16 items so rows longer than that split."""
     _lib.set_param("spmm_min_items", 16)
     _lib.set_param("spmm_max_chunks", 1 << 40)
+    _lib.set_param("spmm_split_min", 0)
     yield
     _lib.set_param("spmm_min_items", 32)
     _lib.set_param("spmm_max_chunks", 0)
+    _lib.set_param("spmm_split_min", 512)
 
 
 def test_config1_update_all_u_mul_e_sum(orc):
