@@ -111,6 +111,25 @@ int bgl_gspmm(const int64_t *indptr, const int32_t *indices, const int32_t *eid,
               int dtype, int op, int reduce, int flags, void *workspace, size_t workspace_bytes,
               void *stream);
 
+/* gSpMM without a caller workspace.  No counterpart in the reference: it is
+ * for callers that cannot allocate device memory (a plugin or serving runtime
+ * that hands the library only its input and output buffers, or a request path
+ * where cudaMalloc, which may synchronise the device, is not allowed).  Same
+ * arguments and results as bgl_gspmm; the scratch is a fixed 64 MiB device
+ * array inside the library (bgl_static_scratch_bytes()), held by every GPU
+ * that loads it until exit.  Calls needing more than that fail with
+ * BGL_E_INVALID.  All calls on a device share the array, so calls that may
+ * overlap on the GPU race and must be serialised by the caller.  The first
+ * call on each device resolves the array's address (cudaGetSymbolAddress) and
+ * should come before any stream capture.  Allocates nothing. */
+size_t bgl_static_scratch_bytes(void);
+int bgl_gspmm_static_scratch(const int64_t *indptr, const int32_t *indices, const int32_t *eid,
+                             const int64_t *deg, int64_t num_rows, int64_t num_edges,
+                             const void *lhs, int64_t lhs_width, int64_t lhs_div, const void *rhs,
+                             int64_t rhs_width, int64_t rhs_div, void *out, int64_t dout,
+                             int64_t *arg_u, int64_t *arg_e, int dtype, int op, int reduce,
+                             int flags, void *stream);
+
 /* --------------------------------------------------------------- gsddmm */
 /* Replaces mdgl_gsddmm (src/capi.mojo:70-91 -> src/ported.mojo:204-329):
  *   out[e, k] = op(lhs[T_l(e), .], rhs[T_r(e), .]),  T = u[e] | v[e] | e

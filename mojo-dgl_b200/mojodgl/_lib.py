@@ -46,6 +46,9 @@ SIGNATURES = {
     "bgl_gspmm_workspace_size": ([_I64, _I64, _I64, _INT, _INT], _SZ),
     "bgl_gspmm": ([_P, _P, _P, _P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64, _P, _I64, _P, _P,
                    _INT, _INT, _INT, _INT, _P, _SZ, _P], _INT),
+    "bgl_static_scratch_bytes": ([], _SZ),
+    "bgl_gspmm_static_scratch": ([_P, _P, _P, _P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64, _P,
+                                  _I64, _P, _P, _INT, _INT, _INT, _INT, _P], _INT),
     "bgl_gsddmm": ([_P, _P, _I64, _P, _I64, _I64, _INT, _P, _I64, _I64, _INT, _P, _I64, _I64,
                     _INT, _INT, _P], _INT),
     "bgl_softmax_workspace_size": ([_I64, _I64, _I64, _INT], _SZ),
