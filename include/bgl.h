@@ -176,6 +176,11 @@ int bgl_gather_mm(const void *a, const void *b, const int64_t *idx_b, void *out,
                   int64_t d1, int64_t r, int64_t d2, int dtype, void *workspace,
                   size_t workspace_bytes, void *stream);
 
+/* Device-side status of the tensor-core grouped GEMM: 0, or the code of the
+ * first bounded wait that expired (1-4) since the last call; synchronises
+ * the device and clears the word. */
+int bgl_tc_error(void);
+
 /* ------------------------------------------------------- array primitives */
 /* src/ported.mojo:145-190 */
 size_t bgl_cumsum_workspace_size(int64_t n);

@@ -149,7 +149,8 @@ size_t sort_bytes(int64_t n, int64_t r) {
 
 }  // namespace
 
-GmmLayout gmm_layout(void *ws, int64_t n, int64_t r, bool gather) {
+GmmLayout gmm_layout(void *ws, int64_t n, int64_t d1, int64_t r, int64_t d2, int dtype,
+                     bool gather) {
     Carver c(ws);
     GmmLayout l;
     l.seg_off = c.take<int64_t>(r + 1);
@@ -159,6 +160,10 @@ GmmLayout gmm_layout(void *ws, int64_t n, int64_t r, bool gather) {
     l.keys_sorted = gather ? c.take<int32_t>(n) : nullptr;
     l.iota = gather ? c.take<int32_t>(n) : nullptr;
     l.perm = gather ? c.take<int32_t>(n) : nullptr;
+    const bool tc = gmm_tensor_core_supported(d1, d2, dtype);
+    const size_t elem = dtype == BGL_BF16 ? 2 : 4;
+    l.tc_b = tc ? c.take<char>(size_t(r) * d1 * d2 * elem) : nullptr;
+    l.tc_a = (tc && gather) ? c.take<char>(size_t(n) * d1 * elem) : nullptr;
     l.sort_temp_bytes = gather ? sort_bytes(n, r) : 0;
     l.sort_temp = gather ? c.take<char>(l.sort_temp_bytes) : nullptr;
     l.bytes = c.used + 256;
@@ -203,11 +208,8 @@ using namespace bgl;
 extern "C" {
 
 size_t bgl_segment_mm_workspace_size(int64_t n, int64_t d1, int64_t r, int64_t d2, int dtype) {
-    (void)d1;
-    (void)d2;
-    (void)dtype;
-    if (n < 0 || r < 0) return 0;
-    return gmm_layout(nullptr, n, r, false).bytes;
+    if (n < 0 || r < 0 || d1 < 0 || d2 < 0) return 0;
+    return gmm_layout(nullptr, n, d1, r, d2, dtype, false).bytes;
 }
 
 int bgl_segment_mm(const void *a, const void *b, void *out, const int64_t *seglen, int64_t n,
@@ -217,10 +219,11 @@ int bgl_segment_mm(const void *a, const void *b, void *out, const int64_t *segle
     if (rc) return rc;
     if (n == 0 || d2 == 0) return BGL_OK;
     if (r > 0 && !seglen) return fail(BGL_E_INVALID, "bgl_segment_mm: null seglen");
-    GmmLayout l = gmm_layout(workspace, n, r, false);
+    GmmLayout l = gmm_layout(workspace, n, d1, r, d2, dtype, false);
     if (workspace_bytes < l.bytes) return fail(BGL_E_WORKSPACE, "bgl_segment_mm: workspace too small");
     cudaStream_t s = as_stream(stream);
-    const bool tc = dtype != BGL_F64 && gmm_tensor_core_supported(d1, d2, dtype);
+    const bool tc = dtype != BGL_F64 && gmm_tensor_core_supported(d1, d2, dtype) &&
+                    gmm_tensor_core_fits(n, r, d2);
     l.tile_rows = tc ? 128 : 64;
     k_gmm_schedule<<<1, 32, 0, s>>>(seglen, r, n, l.tile_rows, l.seg_off, l.tile_off);
     BGL_LAUNCH_CHECK();
@@ -239,15 +242,13 @@ int bgl_segment_mm(const void *a, const void *b, void *out, const int64_t *segle
         BGL_CUDA(cudaMemsetAsync(out, 0, size_t(n) * d2 * elem_size(dtype), s));
         return BGL_OK;
     }
+    if (r == 0) return BGL_OK;  // no segment: every row was zeroed above
     return run_gmm(a, b, out, l, n, d1, r, d2, dtype, tc, s);
 }
 
 size_t bgl_gather_mm_workspace_size(int64_t n, int64_t d1, int64_t r, int64_t d2, int dtype) {
-    (void)d1;
-    (void)d2;
-    (void)dtype;
-    if (n < 0 || r < 0) return 0;
-    return gmm_layout(nullptr, n, r, true).bytes;
+    if (n < 0 || r < 0 || d1 < 0 || d2 < 0) return 0;
+    return gmm_layout(nullptr, n, d1, r, d2, dtype, true).bytes;
 }
 
 int bgl_gather_mm(const void *a, const void *b, const int64_t *idx_b, void *out, int64_t n,
@@ -258,7 +259,7 @@ int bgl_gather_mm(const void *a, const void *b, const int64_t *idx_b, void *out,
     if (n == 0 || d2 == 0) return BGL_OK;
     if (r < 1 || !idx_b) return fail(BGL_E_INVALID, "bgl_gather_mm: needs r >= 1 and idx_b");
     if (r >= (int64_t(1) << 31)) return fail(BGL_E_UNSUPPORTED, "bgl_gather_mm: r >= 2^31");
-    GmmLayout l = gmm_layout(workspace, n, r, true);
+    GmmLayout l = gmm_layout(workspace, n, d1, r, d2, dtype, true);
     if (workspace_bytes < l.bytes) return fail(BGL_E_WORKSPACE, "bgl_gather_mm: workspace too small");
     cudaStream_t s = as_stream(stream);
     if (d1 == 0) {
@@ -275,7 +276,8 @@ int bgl_gather_mm(const void *a, const void *b, const int64_t *idx_b, void *out,
     size_t tb = l.sort_temp_bytes;
     BGL_CUDA(cub::DeviceRadixSort::SortPairs(l.sort_temp, tb, l.keys, l.keys_sorted, l.iota,
                                              l.perm, (int)n, 0, bits, s));
-    const bool tc = dtype != BGL_F64 && gmm_tensor_core_supported(d1, d2, dtype);
+    const bool tc = dtype != BGL_F64 && gmm_tensor_core_supported(d1, d2, dtype) &&
+                    gmm_tensor_core_fits(n, r, d2);
     l.tile_rows = tc ? 128 : 64;
     k_gmm_schedule<<<1, 32, 0, s>>>(l.counts, r, n, l.tile_rows, l.seg_off, l.tile_off);
     BGL_LAUNCH_CHECK();

@@ -17,16 +17,20 @@ struct GmmLayout {
     int32_t *keys_sorted;
     int32_t *iota;
     int32_t *perm;
+    void *tc_b;  // tensor-core path: K-major copy of B (r x d2 x d1)
+    void *tc_a;  // tensor-core gather_mm: A's rows grouped by relation
     void *sort_temp;
     size_t sort_temp_bytes;
     int64_t tile_rows;
     size_t bytes;
 };
 
-GmmLayout gmm_layout(void *ws, int64_t n, int64_t r, bool gather);
+GmmLayout gmm_layout(void *ws, int64_t n, int64_t d1, int64_t r, int64_t d2, int dtype,
+                     bool gather);
 
 // tcgen05 path (grouped_mm_tc.cu).
 bool gmm_tensor_core_supported(int64_t d1, int64_t d2, int dtype);
+bool gmm_tensor_core_fits(int64_t n, int64_t r, int64_t d2);
 int gmm_tensor_core(const void *a, const void *b, void *out, const GmmLayout &l, int64_t n,
                     int64_t d1, int64_t r, int64_t d2, int dtype, cudaStream_t s);
 

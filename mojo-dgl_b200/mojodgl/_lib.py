@@ -57,6 +57,7 @@ SIGNATURES = {
     "bgl_segment_mm": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _INT, _P, _SZ, _P], _INT),
     "bgl_gather_mm_workspace_size": ([_I64, _I64, _I64, _I64, _INT], _SZ),
     "bgl_gather_mm": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _INT, _P, _SZ, _P], _INT),
+    "bgl_tc_error": ([], _INT),
     "bgl_cumsum_workspace_size": ([_I64], _SZ),
     "bgl_cumsum_i64": ([_P, _P, _I64, _P, _SZ, _P], _INT),
     "bgl_clamp_i64": ([_P, _P, _I64, _I64, _I64, _P], _INT),
