@@ -403,6 +403,168 @@ def run_ours(args):
     return 0
 
 
+# ------------------------------------------------------------------- suite
+def make_cfg2(seed=2, n=1_000_000, mean=16, cap=50_000):
+    """Config 2: Zipf(2.1) in-degrees capped at 50,000, rescaled
+    to mean 16 keeping the cap, largest-remainder rounding; uniform sources;
+    edges shuffled."""
+    rng = np.random.default_rng(seed)
+    x = np.minimum(rng.zipf(2.1, n), cap).astype(np.float64)
+    total = mean * n
+    for _ in range(100):
+        capped = x >= cap
+        free = x[~capped].sum()
+        scale = (total - cap * capped.sum()) / free
+        y = np.where(capped, float(cap), np.minimum(x * scale, float(cap)))
+        if np.allclose(y, x):
+            break
+        x = y
+    deg = np.floor(x).astype(np.int64)
+    short = total - int(deg.sum())
+    if short > 0:
+        deg[np.argsort(-(x - deg), kind="stable")[:short]] += 1
+    v = np.repeat(np.arange(n, dtype=np.int64), deg)
+    u = rng.integers(0, n, v.size, dtype=np.int64)
+    p = rng.permutation(v.size)
+    return u[p], v[p]
+
+
+def make_cfg5(seed=5, n=5_000_000, e=50_000_000):
+    """Config 5: uniform edges; geometric(1/32) segment lengths summing to E."""
+    rng = np.random.default_rng(seed)
+    u = rng.integers(0, n, e, dtype=np.int64)
+    v = rng.integers(0, n, e, dtype=np.int64)
+    lens = rng.geometric(1 / 32, size=e // 32 + 1000)
+    c = np.cumsum(lens)
+    k = int(np.searchsorted(c, e)) + 1
+    seglen = lens[:k].copy()
+    seglen[-1] -= int(c[k - 1] - e)
+    return u, v, seglen
+
+
+def run_suite(args):
+    """Every hot-path op at its BASELINE config's full size, inputs resident
+    in HBM, CUDA-event timing (median of --steps after --warmup); one JSON
+    line per op with its algorithmic bytes (gathered model) or FLOPs and the
+    fraction of the measured peak."""
+    import torch
+
+    import mojodgl as dgl
+    from mojodgl import ops
+
+    peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    hbm, tc_peak = float(peaks["hbm_gbs"]), float(peaks["bf16_tflops"])
+    gen = torch.Generator("cuda")
+
+    def t_ms(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(args.steps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1))
+        return statistics.median(times)
+
+    def emit(cfg, op, ms, nbytes, units=None, flops=None, extra=None):
+        rec = {"suite": cfg, "op": op, "ms": round(ms, 4), "alg_bytes": nbytes,
+               "GBps": round(nbytes / ms / 1e6, 1), "frac_hbm": round(nbytes / ms / 1e6 / hbm, 3)}
+        if units:
+            rec["Gedge_feat_s"] = round(units / ms / 1e6, 1)
+        if flops:
+            rec["TFLOPs"] = round(flops / ms / 1e9, 1)
+        if extra:
+            rec.update(extra)
+        print(json.dumps(rec), flush=True)
+
+    want = set(args.suite.split(",")) if args.suite != "all" else {"cfg2", "cfg3", "cfg4", "cfg5"}
+    if "cfg2" in want:
+        u, v = make_cfg2()
+        n, e = 1_000_000, u.size
+        g = dgl.graph((u, v), num_nodes=n)
+        g._device()
+        gen.manual_seed(2)
+        el = torch.randn((n, 8, 1), device="cuda", generator=gen)
+        er = torch.randn((n, 8, 1), device="cuda", generator=gen)
+        feat = torch.randn((n, 8, 64), device="cuda", generator=gen)
+        s = ops.u_add_v(g, el, er)
+        emit("cfg2", "gsddmm u_add_v (N,8,1)", t_ms(lambda: ops.u_add_v(g, el, er)),
+             e * (2 * 32 + 8 + 32), units=e * 8)
+        a = torch.nn.functional.leaky_relu(s, 0.2)
+        emit("cfg2", "edge_softmax dst (E,8,1)", t_ms(lambda: ops.edge_softmax(g, a)),
+             e * (32 + 32 + 4) + n * 8 + (n + 1) * 8, units=e * 8)
+        att = ops.edge_softmax(g, a)
+        emit("cfg2", "gspmm u_mul_e_sum (N,8,64)x(E,8,1)", t_ms(lambda: ops.u_mul_e_sum(g, feat, att)),
+             e * (2048 + 32 + 4 + 4) + n * 2048 + (n + 1) * 8, units=e * 512,
+             extra={"max_in_degree": int(np.bincount(v).max())})
+        del g, el, er, feat, s, a, att
+        torch.cuda.empty_cache()
+    if "cfg3" in want:
+        c = CFG3
+        u, v, h = make_cfg3(**c)
+        n, e, d = c["num_nodes"], c["num_edges"], c["dim"]
+        g = dgl.graph((u, v), num_nodes=n)
+        g._device()
+        hd = torch.from_numpy(h).cuda()
+        for red in ("sum", "mean", "max"):
+            emit("cfg3", "gspmm copy_u_" + red, t_ms(lambda: ops.gspmm(g, "copy_lhs", red, hd, None)),
+                 algorithmic_bytes(n, e, d), units=e * d)
+        emit("cfg3", "gspmm copy_u_max + arg_u (int64)",
+             t_ms(lambda: ops.spmm._gspmm(g, "copy_lhs", "max", hd, None)),
+             algorithmic_bytes(n, e, d, arg=True), units=e * d)
+        gen.manual_seed(3)
+        ef = torch.empty((e, d), device="cuda").uniform_(-1, 1, generator=gen)
+        emit("cfg3", "gspmm u_mul_e_sum (E,128) edge feature", t_ms(lambda: ops.u_mul_e_sum(g, hd, ef)),
+             algorithmic_bytes(n, e, d) + e * d * 4 + e * 4, units=e * d)
+        del g, hd, ef
+        torch.cuda.empty_cache()
+    if "cfg4" in want:
+        rng = np.random.default_rng(4)
+        n, r, d = 2_000_000, 64, 256
+        gen.manual_seed(4)
+        a = torch.empty((n, d), device="cuda").normal_(0, 0.05, generator=gen)
+        b = torch.empty((r, d, d), device="cuda").normal_(0, 0.05, generator=gen)
+        seglen = rng.multinomial(n, rng.dirichlet(0.5 * np.ones(r)))
+        idx = torch.from_numpy(rng.integers(0, r, n)).cuda()
+        flops = 2 * n * d * d
+        for dt, name in ((torch.float32, "fp32 (TF32)"), (torch.bfloat16, "bf16")):
+            aa, bb = a.to(dt), b.to(dt)
+            el = 4 if dt == torch.float32 else 2
+            emit("cfg4", "segment_mm " + name, t_ms(lambda: ops.segment_mm(aa, bb, seglen)),
+                 n * d * el * 2 + r * d * d * el, flops=flops,
+                 extra={"frac_tensor": None})
+            emit("cfg4", "gather_mm " + name, t_ms(lambda: ops.gather_mm(aa, bb, idx_b=idx)),
+                 n * d * el * 2 + r * d * d * el + n * 8, flops=flops)
+        del a, b, aa, bb, idx
+        torch.cuda.empty_cache()
+    if "cfg5" in want:
+        u, v, seglen = make_cfg5()
+        n, e = 5_000_000, u.size
+        g = dgl.graph((u, v), num_nodes=n)
+        g._device()
+        gen.manual_seed(5)
+        U = torch.randn((n, 256), device="cuda", generator=gen)
+        V = torch.randn((n, 256), device="cuda", generator=gen)
+        emit("cfg5", "gsddmm u_dot_v (N,256)", t_ms(lambda: ops.u_dot_v(g, U, V)),
+             e * (2 * 1024 + 8 + 4), units=e * 256)
+        del U, V, g
+        torch.cuda.empty_cache()
+        val = torch.randn((e, 64), device="cuda", generator=gen)
+        sl = torch.from_numpy(seglen).cuda()
+        ns = seglen.size
+        emit("cfg5", "segment_softmax (E,64)", t_ms(lambda: ops.segment_softmax(sl, val)),
+             2 * e * 256 + (ns + 1) * 8, units=e * 64, extra={"segments": ns})
+        for red in ("sum", "max"):
+            emit("cfg5", "segment_reduce " + red + " (E,64)",
+                 t_ms(lambda: ops.segment_reduce(sl, val, red)),
+                 e * 256 + ns * 256 + (ns + 1) * 8, units=e * 64)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -412,6 +574,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     ap.add_argument("--no-extra", action="store_true", help="skip the other ops of the config")
+    ap.add_argument("--suite", default="",
+                    help="time every op of the named configs (cfg2,cfg3,cfg4,cfg5 or all) instead")
     ap.add_argument("--scale", type=float, default=1.0,
                     help="scale the edge count (a smaller case for profiling; nodes unchanged)")
     args = ap.parse_args()
@@ -419,6 +583,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.suite:
+        return run_suite(args)
     return run_ours(args)
 
 
