@@ -482,9 +482,11 @@ def run_suite(args):
         print(json.dumps(rec), flush=True)
 
     want = set(args.suite.split(",")) if args.suite != "all" else {"cfg2", "cfg3", "cfg4", "cfg5"}
+    sc = args.suite_scale
     if "cfg2" in want:
-        u, v = make_cfg2()
-        n, e = 1_000_000, u.size
+        n = int(1_000_000 * sc)
+        u, v = make_cfg2(n=n)
+        e = u.size
         g = dgl.graph((u, v), num_nodes=n)
         g._device()
         gen.manual_seed(2)
@@ -542,8 +544,8 @@ def run_suite(args):
         del a, b, aa, bb, idx
         torch.cuda.empty_cache()
     if "cfg5" in want:
-        u, v, seglen = make_cfg5()
-        n, e = 5_000_000, u.size
+        u, v, seglen = make_cfg5(n=int(5_000_000 * sc), e=int(50_000_000 * sc))
+        n, e = int(5_000_000 * sc), u.size
         g = dgl.graph((u, v), num_nodes=n)
         g._device()
         gen.manual_seed(5)
@@ -576,6 +578,8 @@ def main():
     ap.add_argument("--no-extra", action="store_true", help="skip the other ops of the config")
     ap.add_argument("--suite", default="",
                     help="time every op of the named configs (cfg2,cfg3,cfg4,cfg5 or all) instead")
+    ap.add_argument("--suite-scale", type=float, default=1.0,
+                    help="scale configs 2 and 5 (nodes and edges) in --suite (profiling cases)")
     ap.add_argument("--scale", type=float, default=1.0,
                     help="scale the edge count (a smaller case for profiling; nodes unchanged)")
     args = ap.parse_args()

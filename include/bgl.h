@@ -146,8 +146,11 @@ int bgl_gsddmm(const int32_t *u, const int32_t *v, int64_t num_edges, const void
  * per CSR row and per column h < d, over the row's edges e = eid[i] (eid NULL:
  * e = i) that `mask` selects (mask NULL: all),
  *   out[e, h] = exp(logits[e, h] - max) / sum exp(logits[., h] - max).
- * Rows with no selected edge write nothing.  Row bounds are clamped into
- * [0, num_items] (src/ported.mojo:694-699). */
+ * Rows with no selected edge write nothing.  indptr must be non-decreasing
+ * with indptr[0] = 0 and indptr[num_rows] = num_items (the compat layer turns
+ * the reference's clamped offsets, src/ported.mojo:694-699, into such a CSR).
+ * Heavy rows are split over merge-path chunks; the workspace holds the chunk
+ * boundaries and the split rows' per-column (max, sum) pieces. */
 size_t bgl_softmax_workspace_size(int64_t num_rows, int64_t num_items, int64_t d, int dtype);
 int bgl_edge_softmax(const int64_t *indptr, const int32_t *eid, const int8_t *mask,
                      int64_t num_rows, int64_t num_items, const void *logits, void *out,

@@ -152,6 +152,40 @@ struct Operand {
     bool uniform;  // div % V == 0: one element serves a whole output vector
 };
 
+// Where a lane's V output columns [k0, k0 + V) live in an operand row:
+// resolved once per lane (its columns do not change while it walks edges), so
+// the broadcast's divide and modulo stay out of the gather loop.
+template <int V>
+struct ColMap {
+    int32_t off;  // operand column of the lane's first output column
+    int32_t k0;   // the lane's first output column (for the rare per-element broadcast)
+};
+
+template <typename T, int V>
+__device__ __forceinline__ ColMap<V> col_map(const Operand<T> &o, int64_t k0) {
+    ColMap<V> m;
+    m.k0 = (int32_t)k0;
+    m.off = o.full ? (int32_t)k0 : (int32_t)((k0 / o.div) % o.width);
+    return m;
+}
+
+// Loads the lane's V output columns of operand row `row`.
+template <typename T, int V>
+__device__ __forceinline__ void load_mapped(const Operand<T> &o, int64_t row, const ColMap<V> &m,
+                                            T (&r)[V]) {
+    const T *base = o.ptr + row * o.width;
+    if (o.full) {
+        ld_stream(base + m.off, r);
+    } else if (o.uniform) {
+        T x = __ldg(base + m.off);
+#pragma unroll
+        for (int i = 0; i < V; ++i) r[i] = x;
+    } else {
+#pragma unroll
+        for (int i = 0; i < V; ++i) r[i] = __ldg(base + ((m.k0 + i) / o.div) % o.width);
+    }
+}
+
 // Loads output columns [k0, k0 + V) of operand row `row`.
 template <typename T, int V>
 __device__ __forceinline__ void load_cols(const Operand<T> &o, int64_t row, int64_t k0,

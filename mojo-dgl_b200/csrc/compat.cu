@@ -199,9 +199,12 @@ int softmax_host(const std::vector<int64_t> &indptr, const int32_t *ids, int64_t
     if (mask) TRY(h2d(d_mask.p, mask, size_t(mask_len)));
     TRY(h2d(d_log.p, hf(logits), size_t(rows) * d * 8));
     TRY(h2d(d_out.p, hf(dst), size_t(rows) * d * 8));
+    const int64_t items = indptr[num_rows];  // every row's items lie in [0, items)
+    const size_t wsb = bgl_softmax_workspace_size(num_rows, items, d, BGL_F64);
+    STAGE(d_ws, wsb);
     TRY(bgl_edge_softmax(d_indptr.as<int64_t>(), ids ? d_ids.as<int32_t>() : nullptr,
-                         mask ? d_mask.as<int8_t>() : nullptr, num_rows, n_ids ? n_ids : rows,
-                         d_log.p, d_out.p, d, BGL_F64, nullptr, 0, nullptr));
+                         mask ? d_mask.as<int8_t>() : nullptr, num_rows, items, d_log.p, d_out.p,
+                         d, BGL_F64, d_ws.p, wsb, nullptr));
     BGL_CUDA(cudaDeviceSynchronize());
     return d2h(hfm(dst), d_out.p, size_t(rows) * d * 8);
 }

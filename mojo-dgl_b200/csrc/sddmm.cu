@@ -41,6 +41,11 @@ __global__ void __launch_bounds__(256) k_sddmm(const SddmmArgs<T> a) {
     const int64_t teams = ((int64_t)gridDim.x * blockDim.x) / ts;
     constexpr bool NEED_L = OP != BGL_OP_COPY_RHS;
     constexpr bool NEED_R = OP != BGL_OP_COPY_LHS;
+    ColMap<V> lmap, rmap;
+    if (OP != BGL_OP_DOT) {
+        if (NEED_L) lmap = col_map<T, V>(a.lhs, (int64_t)t * V);
+        if (NEED_R) rmap = col_map<T, V>(a.rhs, (int64_t)t * V);
+    }
     for (int64_t e = team; e < a.num_edges; e += teams) {
         const int64_t li = NEED_L ? target_row(a.lt, a.u, a.v, e) : 0;
         const int64_t ri = NEED_R ? target_row(a.rt, a.u, a.v, e) : 0;
@@ -61,8 +66,13 @@ __global__ void __launch_bounds__(256) k_sddmm(const SddmmArgs<T> a) {
             const int64_t cvn = a.dout / V;
             for (int64_t cv = t; cv < cvn; cv += ts) {
                 T l[V], r[V], o[V];
-                if (NEED_L) load_cols<T, V>(a.lhs, li, cv * V, l);
-                if (NEED_R) load_cols<T, V>(a.rhs, ri, cv * V, r);
+                if (cv == t) {  // the lane's first columns: the common, one-vector case
+                    if (NEED_L) load_mapped<T, V>(a.lhs, li, lmap, l);
+                    if (NEED_R) load_mapped<T, V>(a.rhs, ri, rmap, r);
+                } else {
+                    if (NEED_L) load_cols<T, V>(a.lhs, li, cv * V, l);
+                    if (NEED_R) load_cols<T, V>(a.rhs, ri, cv * V, r);
+                }
 #pragma unroll
                 for (int i = 0; i < V; ++i)
                     o[i] = message<OP, T>(NEED_L ? l[i] : T(0), NEED_R ? r[i] : T(0));

@@ -7,6 +7,7 @@ namespace bgl {
 struct SpmmPlan {
     int vmax;     // widest vector the row width allows
     int ts;       // lanes per team
+    int slices;   // column slices of ts * vmax columns (one team each)
     int64_t num_chunks;
     int64_t items;
     int64_t split_min;
@@ -23,9 +24,12 @@ static SpmmPlan spmm_plan(int64_t n, int64_t e, int64_t dout, int dtype, int red
     p.vmax = (dout % vm == 0) ? vm : 1;
     int64_t cvn = p.vmax ? dout / p.vmax : dout;
     p.ts = next_pow2(cvn < 1 ? 1 : cvn);
+    p.slices = (int)((cvn + p.ts - 1) / p.ts);
+    if (p.slices < 1) p.slices = 1;
     int64_t total = n + e;
     int64_t teams_per_warp = 32 / p.ts;
-    int64_t target = int64_t(num_sms()) * 48 * teams_per_warp * 3;
+    int64_t target = int64_t(num_sms()) * 48 * teams_per_warp * 3 / p.slices;
+    if (target < int64_t(num_sms()) * 8) target = int64_t(num_sms()) * 8;
     // bound the split-row piece buffers to ~256 MB
     size_t elem = (dtype == BGL_F32 ? 4 : 8) + ((reduce == BGL_RED_MAX || reduce == BGL_RED_MIN) ? 4 : 0);
     int64_t per_chunk = 2 * (dout > 0 ? dout : 1) * (int64_t)elem;
@@ -93,8 +97,10 @@ static int run_spmm(const int64_t *indptr, const int32_t *indices, const int32_t
     if (V > 1 && (!aligned(out, vb) || (need_l && lfull && !aligned(lhs, vb)) ||
                   (need_r && rfull && !aligned(rhs, vb))))
         V = 1;
+    // the plan's slices assume its vector width; with V = 1 a team covers
+    // ts columns, so the slice count grows accordingly
     const int64_t cvn = dout / V;
-    const int J = cvn > p.ts ? 4 : 1;
+    const int slices = (int)((cvn + p.ts - 1) / p.ts);
 
     SpmmArgs<T> a;
     a.indptr = indptr;
@@ -112,6 +118,7 @@ static int run_spmm(const int64_t *indptr, const int32_t *indices, const int32_t
     a.mean = red == BGL_RED_MEAN;
     a.zero_inf = (flags & BGL_ZERO_INF) != 0;
     a.ts = p.ts;
+    a.num_slices = slices;
     a.num_chunks = p.num_chunks;
     a.coords = l.coords;
     a.head_val = l.head_val;
@@ -125,8 +132,8 @@ static int run_spmm(const int64_t *indptr, const int32_t *indices, const int32_t
     k_spmm_coords<<<cg, 256, 0, s>>>(indptr, n, e, p.items, p.split_min, p.num_chunks, l.coords);
     BGL_LAUNCH_CHECK();
     constexpr int VM = sizeof(T) == 4 ? 4 : 2;
-    if (V == 1) return J == 1 ? launch_spmm_vj<T, 1, 1>(a, op, red, s) : launch_spmm_vj<T, 1, 4>(a, op, red, s);
-    return J == 1 ? launch_spmm_vj<T, VM, 1>(a, op, red, s) : launch_spmm_vj<T, VM, 4>(a, op, red, s);
+    if (V == 1) return launch_spmm_vj<T, 1, 1>(a, op, red, s);
+    return launch_spmm_vj<T, VM, 1>(a, op, red, s);
 }
 
 }  // namespace bgl

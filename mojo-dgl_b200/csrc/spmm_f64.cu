@@ -7,12 +7,14 @@ namespace {
 
 template <typename T, int OP, int RED, int V, int J>
 int launch_one(const SpmmArgs<T> &a, cudaStream_t s) {
-    int64_t threads = a.num_chunks * a.ts;
+    int64_t threads = a.num_chunks * a.num_slices * a.ts;
     int grid = (int)((threads + 255) / 256);
     if (grid < 1) grid = 1;
     k_spmm<T, OP, RED, V, J><<<grid, 256, 0, s>>>(a);
     BGL_LAUNCH_CHECK();
-    k_spmm_fixup<T, RED, V, J><<<grid, 256, 0, s>>>(a);
+    int fgrid = (int)((a.num_chunks * a.ts + 255) / 256);
+    if (fgrid < 1) fgrid = 1;
+    k_spmm_fixup<T, RED, V, J><<<fgrid, 256, 0, s>>>(a);
     BGL_LAUNCH_CHECK();
     return BGL_OK;
 }
@@ -44,8 +46,6 @@ int launch_spmm_vj(const SpmmArgs<T> &a, int op, int red, cudaStream_t s) {
 }
 
 template int launch_spmm_vj<double, 1, 1>(const SpmmArgs<double> &, int, int, cudaStream_t);
-template int launch_spmm_vj<double, 1, 4>(const SpmmArgs<double> &, int, int, cudaStream_t);
 template int launch_spmm_vj<double, 2, 1>(const SpmmArgs<double> &, int, int, cudaStream_t);
-template int launch_spmm_vj<double, 2, 4>(const SpmmArgs<double> &, int, int, cudaStream_t);
 
 }  // namespace bgl

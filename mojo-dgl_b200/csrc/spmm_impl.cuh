@@ -43,6 +43,7 @@ struct SpmmArgs {
     bool mean;
     bool zero_inf;
     int ts;  // lanes per team (power of two <= 32)
+    int32_t num_slices;  // column slices of ts * V columns; one team per (chunk, slice)
     int64_t num_chunks;
     const Coord *coords;  // num_chunks + 1 boundaries
     T *head_val;
@@ -170,10 +171,19 @@ __device__ __forceinline__ void store_piece(const SpmmArgs<T> &a, T *val, int32_
 #ifndef BGL_SPMM_MINB
 #define BGL_SPMM_MINB 4  // resident 256-thread blocks per SM the registers must allow
 #endif
+// Ops that gather two rows per edge (u_op_e) keep their own depth and
+// occupancy: twice the loads per edge, twice the registers per edge.
+#ifndef BGL_SPMM_UN_BIN
+#define BGL_SPMM_UN_BIN 2
+#endif
+#ifndef BGL_SPMM_MINB_BIN
+#define BGL_SPMM_MINB_BIN 4
+#endif
 template <int OP, int J>
 struct InFlight {
-    static constexpr int both = (OP != BGL_OP_COPY_LHS && OP != BGL_OP_COPY_RHS) ? 2 : 1;
-    static constexpr int value = J == 1 ? BGL_SPMM_UN : (2 / both > 0 ? 2 / both : 1);
+    static constexpr bool both = OP != BGL_OP_COPY_LHS && OP != BGL_OP_COPY_RHS;
+    static constexpr int value = both ? BGL_SPMM_UN_BIN : BGL_SPMM_UN;
+    static constexpr int minb = both ? BGL_SPMM_MINB_BIN : BGL_SPMM_MINB;
 };
 
 // The main pass.  A team walks its chunk's edge range [c0.y, c1.y) in full
@@ -183,13 +193,17 @@ struct InFlight {
 // rows are still arriving.  Row ends are handled as the group is folded, in
 // CSR order, so the arithmetic is exactly the per-row sequential fold.
 template <typename T, int OP, int RED, int V, int J>
-__global__ void __launch_bounds__(256, (J == 1 ? BGL_SPMM_MINB : 2)) k_spmm(const SpmmArgs<T> a) {
+__global__ void __launch_bounds__(256, (InFlight<OP, J>::minb)) k_spmm(const SpmmArgs<T> a) {
     constexpr int UN = InFlight<OP, J>::value;
     constexpr bool NEED_L = OP != BGL_OP_COPY_RHS;
     constexpr bool NEED_R = OP != BGL_OP_COPY_LHS;
     const int ts = a.ts;
     const int t = threadIdx.x & (ts - 1);
-    const int64_t chunk = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) / ts;
+    const int64_t team = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) / ts;
+    // wide rows are cut into column slices, one team per (chunk, slice): the
+    // slices of a chunk walk the same edges, and their id loads share L1/L2
+    const int64_t chunk = team / a.num_slices;
+    const int32_t slice = (int32_t)(team % a.num_slices);
     if (chunk >= a.num_chunks) return;
     // rows and edges are below 2^31 (checked by the host), so the walk
     // bookkeeping stays in 32-bit registers
@@ -200,7 +214,7 @@ __global__ void __launch_bounds__(256, (J == 1 ? BGL_SPMM_MINB : 2)) k_spmm(cons
     const int64_t *__restrict__ indptr = a.indptr;
 
     int32_t head_row = -1, tail_row = -1;
-    for (int32_t cb = 0; cb < cvn; cb += ts * J) {
+    for (int32_t cb = slice * ts * J; cb < cvn; cb += a.num_slices * ts * J) {
         int32_t x = x0;
         if (x >= nrows) break;  // an empty trailing chunk
         int32_t rs = (int32_t)indptr[x];
@@ -237,6 +251,14 @@ __global__ void __launch_bounds__(256, (J == 1 ? BGL_SPMM_MINB : 2)) k_spmm(cons
                 }
         };
 
+        // this lane's columns in each operand, fixed for the whole walk (J = 1)
+        ColMap<V> lmap[J], rmap[J];
+#pragma unroll
+        for (int j = 0; j < J; ++j) {
+            const int64_t k0 = (int64_t)(cb + t + j * ts) * V;
+            if (NEED_L) lmap[j] = col_map<T, V>(a.lhs, k0);
+            if (NEED_R) rmap[j] = col_map<T, V>(a.rhs, k0);
+        }
         int32_t src[UN], edg[UN];
         auto fetch_ids = [&](int32_t e0, int32_t(&s)[UN], int32_t(&d)[UN]) {
 #pragma unroll
@@ -258,8 +280,8 @@ __global__ void __launch_bounds__(256, (J == 1 ? BGL_SPMM_MINB : 2)) k_spmm(cons
                     for (int j = 0; j < J; ++j) {
                         const int32_t cv = cb + t + j * ts;
                         if (cv < cvn) {
-                            if (NEED_L) load_cols<T, V>(a.lhs, src[u], (int64_t)cv * V, lv[u][j]);
-                            if (NEED_R) load_cols<T, V>(a.rhs, edg[u], (int64_t)cv * V, rv[u][j]);
+                            if (NEED_L) load_mapped<T, V>(a.lhs, src[u], lmap[j], lv[u][j]);
+                            if (NEED_R) load_mapped<T, V>(a.rhs, edg[u], rmap[j], rv[u][j]);
                         }
                     }
                 }
@@ -294,7 +316,7 @@ __global__ void __launch_bounds__(256, (J == 1 ? BGL_SPMM_MINB : 2)) k_spmm(cons
             tail_row = x;
         }
     }
-    if (t == 0) {
+    if (t == 0 && slice == 0) {
         a.head_row[chunk] = head_row;
         a.tail_row[chunk] = tail_row;
     }

@@ -76,8 +76,10 @@ def edge_softmax(graph, logits, eids=ALL, norm_by="dst"):
         lt = T.to_dev(logits, dtype).reshape(out_len, d)[:k].contiguous()
     out = torch.zeros((out_len, d), dtype=dtype, device=T.device())
     if num_rows and num_items and d:
+        nbytes = lib().bgl_softmax_workspace_size(num_rows, num_items, d, T.code_of(dtype))
+        ws = T.workspace(nbytes)
         rc = lib().bgl_edge_softmax(T.ptr(indptr), T.ptr(eid), None, num_rows, num_items,
-                                    T.ptr(lt), T.ptr(out), d, T.code_of(dtype), None, 0,
+                                    T.ptr(lt), T.ptr(out), d, T.code_of(dtype), T.ptr(ws), nbytes,
                                     T.stream())
         check(rc, "edge_softmax")
     return T.result(out.reshape(shape), kind)

@@ -92,8 +92,10 @@ def segment_softmax(seglen, value):
     out = torch.zeros((n, d), dtype=dtype, device=T.device())
     if num_seg and n and d:
         vt = T.to_dev(value, dtype)
+        nbytes = lib().bgl_softmax_workspace_size(num_seg, n, d, T.code_of(dtype))
+        ws = T.workspace(nbytes)
         rc = lib().bgl_edge_softmax(T.ptr(offsets), None, None, num_seg, n, T.ptr(vt), T.ptr(out),
-                                    d, T.code_of(dtype), None, 0, T.stream())
+                                    d, T.code_of(dtype), T.ptr(ws), nbytes, T.stream())
         check(rc, "segment_softmax")
     return T.result(out.reshape(shape), kind)
 

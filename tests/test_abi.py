@@ -93,6 +93,7 @@ def test_gsddmm_and_softmax_validation(lib):
     assert lib.bgl_gsddmm(None, None, 3, None, 1, 1, 7, None, 1, 1, 0, None, 1, 0, 0, 0, None) == 1
     assert lib.bgl_gsddmm(None, None, 3, None, 4, 1, 0, None, 4, 1, 1, None, 2, 4, 0, 4, None) == 1
     assert lib.bgl_edge_softmax(None, None, None, 2, 2, None, None, 1, 0, None, 0, None) == 1
+    assert b"null buffer" in lib.bgl_last_error()
     assert lib.bgl_edge_softmax(None, None, None, 0, 0, None, None, 1, 0, None, 0, None) == 0
     assert lib.bgl_edge_softmax(None, None, None, 1, 1, None, None, 1, 9, None, 0, None) == 3
 

@@ -83,9 +83,13 @@ def test_static_scratch_rejects_oversized_calls():
     lib = _lib.lib()
     cap = lib.bgl_static_scratch_bytes()
     assert cap == 64 << 20
-    # a plan whose split-row piece buffers exceed the fixed scratch
-    rc = lib.bgl_gspmm_static_scratch(None, None, None, None, 10_000_000, 1_000_000_000, None,
-                                      4096, 1, None, 1, 1, None, 4096, None, None, _lib.BGL_F32,
-                                      _lib.OP_COPY_LHS, _lib.REDUCE_SUM, 0, None)
+    # a plan whose split-row piece buffers exceed the fixed scratch: wide
+    # float64 rows with max (values + winning positions per chunk)
+    rows, edges, width = 10_000_000, 1_000_000_000, 8192
+    need = lib.bgl_gspmm_workspace_size(rows, edges, width, _lib.BGL_F64, _lib.REDUCE_MAX)
+    assert need > cap
+    rc = lib.bgl_gspmm_static_scratch(None, None, None, None, rows, edges, None, width, 1, None,
+                                      1, 1, None, width, None, None, _lib.BGL_F64,
+                                      _lib.OP_COPY_LHS, _lib.REDUCE_MAX, 0, None)
     assert rc == 1
     assert b"built-in scratch holds" in lib.bgl_last_error()
