@@ -55,9 +55,15 @@ enum {
 enum { BGL_RED_SUM = 0, BGL_RED_MAX = 1, BGL_RED_MIN = 2, BGL_RED_MEAN = 3 };
 /* gspmm flags */
 enum {
-    BGL_ZERO_INF = 1 /* replace +-inf results with 0 (the max/min post-pass of
-                        python/mojodgl/heterograph.py:232-239 and
-                        python/mojodgl/ops/segment.py:106-110, fused) */
+    BGL_ZERO_INF = 1,  /* replace +-inf results with 0 (the max/min post-pass of
+                          python/mojodgl/heterograph.py:232-239 and
+                          python/mojodgl/ops/segment.py:106-110, fused) */
+    BGL_ACCUMULATE = 2 /* fold each row into what out (and arg_e) already hold:
+                          sums add; max/min keep the better value, a tie going
+                          to the smaller edge id.  Lets one aggregation run as
+                          several passes over disjoint edge subsets (e.g. per
+                          source-owner block as blocks arrive); the mean divide
+                          and ZERO_INF belong on the last pass only */
 };
 
 /* ------------------------------------------------------------- utilities */

@@ -5,18 +5,24 @@
 namespace bgl {
 namespace {
 
-template <typename T, int OP, int RED, int V, int J>
-int launch_one(const SpmmArgs<T> &a, cudaStream_t s) {
+template <typename T, int OP, int RED, int V, int J, bool ACC>
+int launch_kernels(const SpmmArgs<T> &a, cudaStream_t s) {
     int64_t threads = a.num_chunks * a.num_slices * a.ts;
     int grid = (int)((threads + 255) / 256);
     if (grid < 1) grid = 1;
-    k_spmm<T, OP, RED, V, J><<<grid, 256, 0, s>>>(a);
+    k_spmm<T, OP, RED, V, J, ACC><<<grid, 256, 0, s>>>(a);
     BGL_LAUNCH_CHECK();
     int fgrid = (int)((a.num_chunks * a.ts + 255) / 256);
     if (fgrid < 1) fgrid = 1;
-    k_spmm_fixup<T, RED, V, J><<<fgrid, 256, 0, s>>>(a);
+    k_spmm_fixup<T, RED, V, J, ACC><<<fgrid, 256, 0, s>>>(a);
     BGL_LAUNCH_CHECK();
     return BGL_OK;
+}
+
+template <typename T, int OP, int RED, int V, int J>
+int launch_one(const SpmmArgs<T> &a, cudaStream_t s) {
+    return a.accumulate ? launch_kernels<T, OP, RED, V, J, true>(a, s)
+                        : launch_kernels<T, OP, RED, V, J, false>(a, s);
 }
 
 template <typename T, int OP, int V, int J>

@@ -42,6 +42,7 @@ struct SpmmArgs {
     int64_t *arg_e;
     bool mean;
     bool zero_inf;
+    bool accumulate;  // BGL_ACCUMULATE: selects the kernels compiled with ACC = true
     int ts;  // lanes per team (power of two <= 32)
     int32_t num_slices;  // column slices of ts * V columns; one team per (chunk, slice)
     int64_t num_chunks;
@@ -106,8 +107,11 @@ __device__ __forceinline__ void fold(T &acc, int32_t &pos, T m, int32_t p) {
 }
 
 // Writes one finished row: the mean divide, the inf->0 post-pass and the arg
-// indices are all applied here, so the row is written once.
-template <typename T, int RED, int V, int J>
+// indices are all applied here, so the row is written once.  In accumulate
+// mode the row is first folded into what `out` already holds (a partial result
+// over other edges of the same rows): sums add, max/min keep the better value,
+// and on a tie the smaller edge id -- the earlier message in CSR order -- wins.
+template <typename T, int RED, int V, int J, bool ACC>
 __device__ __forceinline__ void emit_row(const SpmmArgs<T> &a, int64_t row, int64_t cb, int t,
                                          int64_t cvn, const T (&acc)[J][V],
                                          const int32_t (&pos)[J][V]) {
@@ -116,26 +120,55 @@ __device__ __forceinline__ void emit_row(const SpmmArgs<T> &a, int64_t row, int6
         int64_t dg = a.deg ? a.deg[row] : a.indptr[row + 1] - a.indptr[row];
         scale = dg < 1 ? T(1) : T(dg);
     }
+    constexpr bool ARG = RED == BGL_RED_MAX || RED == BGL_RED_MIN;
 #pragma unroll
     for (int j = 0; j < J; ++j) {
         int64_t cv = cb + t + (int64_t)j * a.ts;
         if (cv >= cvn) continue;
         int64_t off = row * a.dout + cv * V;
         T o[V];
+        int64_t ae[V], au[V];
+        bool take[V];
 #pragma unroll
         for (int i = 0; i < V; ++i) {
-            T v = acc[j][i];
+            const int32_t p = pos[j][i];
+            ae[i] = p < 0 ? -1 : (a.eid ? (int64_t)a.eid[p] : (int64_t)p);
+            au[i] = (ARG && a.arg_u && p >= 0) ? (int64_t)a.indices[p] : -1;
+            take[i] = true;
+        }
+        if (ACC) {
+            T old[V];
+            load_vec<T, V>(a.out + off, old);
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+                if (ARG) {
+                    const int64_t oe = a.arg_e ? a.arg_e[off + i] : -1;
+                    const T v = acc[j][i];
+                    const bool better = RED == BGL_RED_MAX ? v > old[i] : v < old[i];
+                    take[i] = better || (v == old[i] && ae[i] >= 0 && (oe < 0 || ae[i] < oe));
+                    o[i] = take[i] ? v : old[i];
+                } else {
+                    o[i] = Arith<T>::add(old[i], acc[j][i]);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < V; ++i) o[i] = acc[j][i];
+        }
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+            T v = o[i];
             if (a.mean) v = Arith<T>::div(v, scale);
             if (a.zero_inf && isinf(v)) v = T(0);
             o[i] = v;
         }
         store_vec<T, V>(a.out + off, o);
-        if (RED == BGL_RED_MAX || RED == BGL_RED_MIN) {
+        if (ARG) {
 #pragma unroll
             for (int i = 0; i < V; ++i) {
-                int32_t p = pos[j][i];
-                if (a.arg_u) a.arg_u[off + i] = p < 0 ? -1 : (int64_t)a.indices[p];
-                if (a.arg_e) a.arg_e[off + i] = p < 0 ? -1 : (a.eid ? (int64_t)a.eid[p] : (int64_t)p);
+                if (!take[i]) continue;
+                if (a.arg_u) a.arg_u[off + i] = au[i];
+                if (a.arg_e) a.arg_e[off + i] = ae[i];
             }
         }
     }
@@ -192,7 +225,7 @@ struct InFlight {
 // and the next group's neighbour ids are fetched while the current group's
 // rows are still arriving.  Row ends are handled as the group is folded, in
 // CSR order, so the arithmetic is exactly the per-row sequential fold.
-template <typename T, int OP, int RED, int V, int J>
+template <typename T, int OP, int RED, int V, int J, bool ACC>
 __global__ void __launch_bounds__(256, (InFlight<OP, J>::minb)) k_spmm(const SpmmArgs<T> a) {
     constexpr int UN = InFlight<OP, J>::value;
     constexpr bool NEED_L = OP != BGL_OP_COPY_RHS;
@@ -233,7 +266,7 @@ __global__ void __launch_bounds__(256, (InFlight<OP, J>::minb)) k_spmm(const Spm
         // earlier chunk) and opens row x + 1
         auto close_row = [&]() {
             if (row_begin == rs) {
-                emit_row<T, RED, V, J>(a, x, cb, t, cvn, acc, pos);
+                emit_row<T, RED, V, J, ACC>(a, x, cb, t, cvn, acc, pos);
             } else {
                 store_piece<T, RED, V, J>(a, a.head_val, a.head_pos, chunk, cb, t, cvn, acc, pos);
                 head_row = x;
@@ -323,7 +356,7 @@ __global__ void __launch_bounds__(256, (InFlight<OP, J>::minb)) k_spmm(const Spm
 }
 
 // Folds the pieces of every split row in CSR order and writes the row.
-template <typename T, int RED, int V, int J>
+template <typename T, int RED, int V, int J, bool ACC>
 __global__ void __launch_bounds__(256) k_spmm_fixup(const SpmmArgs<T> a) {
     const int ts = a.ts;
     const int t = threadIdx.x & (ts - 1);
@@ -361,7 +394,7 @@ __global__ void __launch_bounds__(256) k_spmm_fixup(const SpmmArgs<T> a) {
                 }
             }
         }
-        emit_row<T, RED, V, J>(a, row, cb, t, cvn, acc, pos);
+        emit_row<T, RED, V, J, ACC>(a, row, cb, t, cvn, acc, pos);
     }
 }
 

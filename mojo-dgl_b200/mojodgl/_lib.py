@@ -29,6 +29,7 @@ TARGETS = {"u": SRC_CODE, "v": DST_CODE, "e": EDGE_CODE}
 # include/bgl.h
 BGL_F32, BGL_F64, BGL_BF16 = 0, 1, 2
 BGL_ZERO_INF = 1
+BGL_ACCUMULATE = 2
 
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64

@@ -118,3 +118,121 @@ class DeviceShard:
                               OP_COPY_LHS, red, BGL_ZERO_INF if reduce_op in ("max", "min") else 0,
                               T.ptr(workspace), nbytes, T.stream()), "gspmm")
         return out
+
+
+class OwnerPipeline:
+    """A destination-row shard whose in-edges are split by the owner block of
+    their source, so the halo exchange overlaps the aggregation.
+
+    The features arrive over P - 1 ring steps of NCCL send/recv (step k: send
+    my block to rank + k, receive the block of rank - k); the gSpMM pass over
+    the edges whose sources live in a block runs as soon as that block is in,
+    while the next block is in flight.  Each pass after the first folds into
+    the output (BGL_ACCUMULATE); the mean divide and the max/min inf->0 are
+    applied by the last pass.  Per-owner sub-CSRs keep global edge ids, so
+    max/min ties resolve to the smaller edge id, as in the single-GPU result;
+    sums are the same messages added in owner-block order (compared with a
+    tolerance against the single-GPU order)."""
+
+    def __init__(self, u, v, lo, hi, rank, world, num_nodes):
+        import torch
+
+        from . import _tensor as T
+        from ._lib import check, lib
+
+        self.rank, self.world = rank, world
+        self.lo, self.hi = int(lo), int(hi)
+        self.blk, self.owners = owner_blocks(num_nodes, world)
+        n = self.hi - self.lo
+        sel = np.nonzero((v >= lo) & (v < hi))[0]
+        uu = u[sel]
+        vv = v[sel] - lo
+        owner = uu // self.blk
+        dev = T.device()
+        self.parts = []
+        for p in range(world):
+            m = np.nonzero(owner == p)[0]
+            ne = int(m.size)
+            key = torch.from_numpy(np.ascontiguousarray(vv[m])).to(dev)
+            other = torch.from_numpy(np.ascontiguousarray(uu[m] - p * self.blk)).to(dev)
+            indptr = torch.empty(n + 1, dtype=torch.int64, device=dev)
+            deg = torch.empty(n, dtype=torch.int64, device=dev)
+            order = torch.empty(ne, dtype=torch.int32, device=dev)
+            indices = torch.empty(ne, dtype=torch.int32, device=dev)
+            nbytes = lib().bgl_csr_build_workspace_size(ne, n)
+            ws = T.workspace(nbytes)
+            check(lib().bgl_csr_build(T.ptr(key), T.ptr(other), ne, n, T.ptr(indptr), T.ptr(deg),
+                                      T.ptr(order), T.ptr(indices), T.ptr(ws), nbytes, T.stream()),
+                  "bgl_csr_build")
+            gid = torch.from_numpy(sel[m].astype(np.int64)).to(dev)
+            eid = gid[order.long()].to(torch.int32) if ne else order
+            self.parts.append((indptr, indices, eid, ne))
+        self.deg = torch.from_numpy(np.bincount(vv, minlength=n).astype(np.int64)).to(dev)
+        self.num_rows = n
+
+    def _pass(self, p, feat, out, reduce_op, first, last, arg_e, ws):
+        from . import _tensor as T
+        from ._lib import (BGL_ACCUMULATE, BGL_ZERO_INF, OP_COPY_LHS, REDUCE_SUM, REDUCERS, check,
+                           lib)
+
+        indptr, indices, eid, ne = self.parts[p]
+        d = int(feat.shape[1])
+        red = REDUCERS[reduce_op]
+        if reduce_op == "mean" and not last:
+            red = REDUCE_SUM
+        flags = (0 if first else BGL_ACCUMULATE)
+        if last and reduce_op in ("max", "min"):
+            flags |= BGL_ZERO_INF
+        code = T.code_of(feat.dtype)
+        nbytes = lib().bgl_gspmm_workspace_size(self.num_rows, ne, d, code, red)
+        if ws[0] is None or ws[0].numel() < nbytes:
+            ws[0] = T.workspace(nbytes)
+        check(lib().bgl_gspmm(T.ptr(indptr), T.ptr(indices), T.ptr(eid), T.ptr(self.deg),
+                              self.num_rows, ne, T.ptr(feat), d, 1, None, 1, 1, T.ptr(out), d, None,
+                              T.ptr(arg_e), code, OP_COPY_LHS, red, flags, T.ptr(ws[0]), nbytes,
+                              T.stream()), "gspmm")
+
+    def copy_u(self, my_block, reduce_op, out, arg_e=None, bufs=None, ws=None):
+        """out[rows of this shard] = reduce over in-edges of the source
+        feature; my_block is this rank's (blk, D) feature block."""
+        ws = ws if ws is not None else [None]
+
+        def on_block(owner, block, first, last):
+            self._pass(owner, block, out, reduce_op, first, last, arg_e, ws)
+
+        ring_exchange(my_block, bufs, self.rank, self.world, on_block)
+        return out
+
+
+def ring_exchange(my_block, bufs, rank, world, on_block):
+    """Hand every rank's feature block to on_block(owner, block, first, last),
+    this rank's own block first, then the others as they arrive over P - 1
+    ring steps of send/recv (step k: send to rank + k, receive from rank - k).
+    Step k + 1 is issued before block k is processed, so the transfer of the
+    next block overlaps the work on the current one; the two receive buffers
+    alternate, and a buffer is only refilled once the work issued on it is in
+    the stream order before the receive (torch orders a collective after the
+    work already queued on the current stream)."""
+    import torch
+    import torch.distributed as dist
+
+    P, r = world, rank
+    if P == 1:
+        on_block(r, my_block, True, True)
+        return
+    if bufs is None:
+        bufs = [torch.empty_like(my_block), torch.empty_like(my_block)]
+
+    def issue(k):
+        ops = [dist.P2POp(dist.isend, my_block, (r + k) % P),
+               dist.P2POp(dist.irecv, bufs[k % 2], (r - k) % P)]
+        return dist.batch_isend_irecv(ops)
+
+    works = issue(1)
+    on_block(r, my_block, True, False)
+    for k in range(1, P):
+        for w in works:
+            w.wait()
+        if k + 1 < P:
+            works = issue(k + 1)
+        on_block((r - k) % P, bufs[k % 2], False, k == P - 1)

@@ -311,3 +311,54 @@ def test_compat_abi_matches_the_oracle(orc):
     L.mdgl_replace_inf_with_zero(_addr(f), _addr(a), 4)
     np.testing.assert_array_equal(a, [1.0, 0.0, 0.0, -2.0])
     assert L.bgl_last_error() == b""
+
+
+@pytest.mark.parametrize("red", ["sum", "mean", "max", "min"])
+def test_accumulate_passes_match_one_pass(orc, red):
+    """BGL_ACCUMULATE: the aggregation run as P passes, one per source-owner
+    block (as the multi-GPU halo delivers them), equals the single pass --
+    float64 sums to rtol 1e-12, max/min and their edge ids exactly."""
+    import torch
+
+    L = _lib.lib()
+    u, v = power_law(6000, 91)
+    rng = np.random.default_rng(92)
+    n, d, P = 6000, 8, 3
+    x = rng.integers(-4, 5, size=(n, d)).astype(np.float64) + rng.normal(size=(n, d)) * (red in ("sum", "mean"))
+    blk = (n + P - 1) // P
+    dev = torch.device("cuda")
+    code = _lib.REDUCERS[red]
+    out = torch.empty((n, d), dtype=torch.float64, device=dev)
+    arg_e = torch.empty((n, d), dtype=torch.int64, device=dev)
+    deg = torch.from_numpy(np.bincount(v, minlength=n).astype(np.int64)).to(dev)
+    xs = torch.from_numpy(x).to(dev)
+    for p in range(P):
+        m = np.nonzero(u // blk == p)[0]
+        order = m[np.argsort(v[m], kind="stable")]
+        indptr = np.zeros(n + 1, dtype=np.int64)
+        np.cumsum(np.bincount(v[m], minlength=n), out=indptr[1:])
+        t_ip = torch.from_numpy(indptr).to(dev)
+        t_nbr = torch.from_numpy((u[order] - p * blk).astype(np.int32)).to(dev)
+        t_eid = torch.from_numpy(order.astype(np.int32)).to(dev)
+        feat = xs[p * blk: (p + 1) * blk].contiguous()
+        r = _lib.REDUCE_SUM if (red == "mean" and p < P - 1) else code
+        flags = (_lib.BGL_ACCUMULATE if p else 0) | (
+            _lib.BGL_ZERO_INF if (p == P - 1 and red in ("max", "min")) else 0)
+        nb = L.bgl_gspmm_workspace_size(n, m.size, d, _lib.BGL_F64, r)
+        ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=dev)
+        rc = L.bgl_gspmm(t_ip.data_ptr(), t_nbr.data_ptr(), t_eid.data_ptr(), deg.data_ptr(), n,
+                         m.size, feat.data_ptr(), d, 1, None, 1, 1, out.data_ptr(), d, None,
+                         arg_e.data_ptr() if red in ("max", "min") else None, _lib.BGL_F64,
+                         _lib.OP_COPY_LHS, r, flags, ws.data_ptr(), nb,
+                         torch.cuda.current_stream().cuda_stream)
+        assert rc == 0, L.bgl_last_error()
+    torch.cuda.synchronize()
+    og = orc.Graph(u, v, num_nodes=n)
+    if red in ("max", "min"):
+        want, _, want_e = orc.gspmm(og, "copy_lhs", red, x, None, with_arg=True)
+        want = orc.replace_inf_with_zero(want)
+        np.testing.assert_array_equal(out.cpu().numpy(), want)
+        np.testing.assert_array_equal(arg_e.cpu().numpy(), want_e)
+    else:
+        np.testing.assert_allclose(out.cpu().numpy(), orc.gspmm(og, "copy_lhs", red, x, None),
+                                   rtol=1e-12, atol=1e-12)

@@ -17,7 +17,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from mojodgl.partition import DstShard, assemble_gathered, edge_balanced_ranges, owner_blocks
+from mojodgl.partition import (DstShard, assemble_gathered, edge_balanced_ranges, owner_blocks,
+                               ring_exchange)
 
 
 def graph(seed=5, n=3000):
@@ -97,3 +98,76 @@ def test_two_gloo_ranks_reproduce_the_single_process_result():
     for _, lo, hi, out in results:
         got[lo:hi] = out
     np.testing.assert_array_equal(got, want)
+
+
+def _ring_rank(rank, world, port, q):
+    """The owner-pipelined halo: blocks arrive over the ring and each is
+    reduced over the shard's edges whose sources it owns; sums add in owner
+    order, max keeps the better value with the smaller edge id on a tie."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import sys
+
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        sys.path.insert(0, root)
+        from oracle import oracle as orc
+
+        u, v, h, n = graph(seed=9)
+        bounds = edge_balanced_ranges(np.bincount(v, minlength=n), world)
+        lo, hi = int(bounds[rank]), int(bounds[rank + 1])
+        blk, owners = owner_blocks(n, world)
+        a, b = owners[rank]
+        mine = torch.zeros(blk, h.shape[1], dtype=torch.float64)
+        mine[: b - a] = torch.from_numpy(h[a:b])
+        sel = np.nonzero((v >= lo) & (v < hi))[0]
+        sums = np.zeros((hi - lo, h.shape[1]))
+        best = np.full((hi - lo, h.shape[1]), -np.inf)
+        best_e = np.full((hi - lo, h.shape[1]), -1, dtype=np.int64)
+        seen = []
+
+        def on_block(owner, block, first, last):
+            seen.append(owner)
+            m = sel[(u[sel] // blk) == owner]
+            og = orc.Graph(u[m] - owner * blk, v[m] - lo, num_nodes=max(blk, hi - lo))
+            x = block.numpy()
+            part = orc.gspmm(og, "copy_lhs", "sum", x, None)[: hi - lo]
+            sums[:] = part if first else sums + part
+            mx, au, ae = orc.gspmm(og, "copy_lhs", "max", x, None, with_arg=True)
+            mx, ae = mx[: hi - lo], ae[: hi - lo]
+            ge = np.where(ae >= 0, m[np.maximum(ae, 0)], -1)  # global edge ids
+            take = (mx > best) | ((mx == best) & (ge >= 0) & ((best_e < 0) | (ge < best_e)))
+            best[take] = mx[take]
+            best_e[take] = ge[take]
+
+        ring_exchange(mine, None, rank, world, on_block)
+        q.put((rank, lo, hi, sums, best, best_e, seen))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_ring_halo_reproduces_the_single_process_result(world):
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_ring_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    from oracle import oracle as orc
+
+    u, v, h, n = graph(seed=9)
+    og = orc.Graph(u, v, num_nodes=n)
+    want_sum = orc.gspmm(og, "copy_lhs", "sum", h, None)
+    want_max, _, want_e = orc.gspmm(og, "copy_lhs", "max", h, None, with_arg=True)
+    for rank, lo, hi, sums, best, best_e, seen in results:
+        assert sorted(seen) == list(range(world)) and seen[0] == rank
+        np.testing.assert_allclose(sums, want_sum[lo:hi], rtol=1e-12, atol=1e-12)
+        np.testing.assert_array_equal(best, want_max[lo:hi])
+        np.testing.assert_array_equal(best_e, want_e[lo:hi])
