@@ -152,41 +152,47 @@ struct Operand {
     bool uniform;  // div % V == 0: one element serves a whole output vector
 };
 
-// Where a lane's V output columns [k0, k0 + V) live in an operand row:
-// resolved once per lane (its columns do not change while it walks edges), so
-// the broadcast's divide and modulo stay out of the gather loop.
+// Where a broadcast operand's values for a lane's V output columns
+// [k0, k0 + V) live in its row: resolved once per lane (its columns do not
+// change while it walks edges), so the broadcast's divide and modulo stay out
+// of the gather loop.  A full operand needs no map: its offset is k0 itself,
+// recomputed in the loop, which keeps one less register live.
 template <int V>
 struct ColMap {
-    int32_t off;  // operand column of the lane's first output column
-    int32_t k0;   // the lane's first output column (for the rare per-element broadcast)
+    // uniform broadcast: the one operand column all V outputs read;
+    // otherwise the lane's first output column
+    int32_t off;
 };
 
 template <typename T, int V>
 __device__ __forceinline__ ColMap<V> col_map(const Operand<T> &o, int64_t k0) {
     ColMap<V> m;
-    m.k0 = (int32_t)k0;
-    m.off = o.full ? (int32_t)k0 : (int32_t)((k0 / o.div) % o.width);
+    m.off = (o.full || !o.uniform) ? (int32_t)k0
+                                   : (int32_t)(((uint32_t)k0 / (uint32_t)o.div) % (uint32_t)o.width);
     return m;
 }
 
-// Loads the lane's V output columns of operand row `row`.
+// Loads the lane's V output columns [k0, k0 + V) of operand row `row`.
 template <typename T, int V>
-__device__ __forceinline__ void load_mapped(const Operand<T> &o, int64_t row, const ColMap<V> &m,
-                                            T (&r)[V]) {
+__device__ __forceinline__ void load_mapped(const Operand<T> &o, int64_t row, int64_t k0,
+                                            const ColMap<V> &m, T (&r)[V]) {
     const T *base = o.ptr + row * o.width;
     if (o.full) {
-        ld_stream(base + m.off, r);
+        ld_stream(base + k0, r);
     } else if (o.uniform) {
         T x = __ldg(base + m.off);
 #pragma unroll
         for (int i = 0; i < V; ++i) r[i] = x;
     } else {
 #pragma unroll
-        for (int i = 0; i < V; ++i) r[i] = __ldg(base + ((m.k0 + i) / o.div) % o.width);
+        for (int i = 0; i < V; ++i)
+            r[i] = __ldg(base + ((uint32_t)(m.off + i) / (uint32_t)o.div) % (uint32_t)o.width);
     }
 }
 
-// Loads output columns [k0, k0 + V) of operand row `row`.
+// Loads output columns [k0, k0 + V) of operand row `row`.  Row widths and
+// broadcast divisors are below 2^31, so the broadcast's column arithmetic is
+// done in 32-bit unsigned integers (a fraction of the 64-bit divide's cost).
 template <typename T, int V>
 __device__ __forceinline__ void load_cols(const Operand<T> &o, int64_t row, int64_t k0,
                                           T (&r)[V]) {
@@ -194,12 +200,13 @@ __device__ __forceinline__ void load_cols(const Operand<T> &o, int64_t row, int6
     if (o.full) {
         ld_stream(base + k0, r);
     } else if (o.uniform) {
-        T x = __ldg(base + (k0 / o.div) % o.width);
+        T x = __ldg(base + ((uint32_t)k0 / (uint32_t)o.div) % (uint32_t)o.width);
 #pragma unroll
         for (int i = 0; i < V; ++i) r[i] = x;
     } else {
 #pragma unroll
-        for (int i = 0; i < V; ++i) r[i] = __ldg(base + ((k0 + i) / o.div) % o.width);
+        for (int i = 0; i < V; ++i)
+            r[i] = __ldg(base + ((uint32_t)(k0 + i) / (uint32_t)o.div) % (uint32_t)o.width);
     }
 }
 
@@ -211,6 +218,71 @@ inline int next_pow2(int64_t x) {
     int p = 1;
     while (p < x && p < 32) p <<= 1;
     return p;
+}
+
+// ------------------------------------------------------- async row staging
+// Per-lane asynchronous copies global -> shared (cp.async, sm_80 and later).
+// A lane copies its own V columns of a gathered row into its own shared slot
+// and later reads back only what it copied, so the per-thread
+// cp.async.wait_group is the only synchronisation: no barrier, no spin.  The
+// data in flight holds no registers, so the copy depth is bounded by shared
+// memory instead of the register file.
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+// 16-byte copies bypass L1 (.cg), like ld_stream: gathered rows are read once.
+template <int BYTES>
+__device__ __forceinline__ void cp_async(uint32_t dst, const void *src) {
+    static_assert(BYTES == 4 || BYTES == 8 || BYTES == 16, "cp.async copies 4, 8 or 16 bytes");
+    if (BYTES == 16)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+    else
+        asm volatile("cp.async.ca.shared.global [%0], [%1], %2;" ::"r"(dst), "l"(src), "n"(BYTES)
+                     : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+// Returns once at most N of this thread's committed groups are still pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Starts the copy of the lane's V output columns [k0, k0 + V) of operand row
+// `row` into shared slot `dst` (V * sizeof(T) bytes, aligned to that size).
+// A uniform broadcast copies its one element; a non-uniform one copies each.
+template <typename T, int V>
+__device__ __forceinline__ void stage_cols(const Operand<T> &o, int64_t row, int64_t k0,
+                                           const ColMap<V> &m, uint32_t dst) {
+    const T *base = o.ptr + row * o.width;
+    if (o.full) {
+        cp_async<V * sizeof(T)>(dst, base + k0);
+    } else if (o.uniform) {
+        cp_async<sizeof(T)>(dst, base + m.off);
+    } else {
+#pragma unroll
+        for (int i = 0; i < V; ++i)
+            cp_async<sizeof(T)>(dst + i * sizeof(T),
+                                base + ((uint32_t)(m.off + i) / (uint32_t)o.div) % (uint32_t)o.width);
+    }
+}
+
+// Reads back what stage_cols copied into `slot`.
+template <typename T, int V>
+__device__ __forceinline__ void read_cols(const Operand<T> &o, const T *slot, T (&r)[V]) {
+    if (o.full || !o.uniform) {
+        using VT = typename VecT<T, V>::type;
+        const VT v = *reinterpret_cast<const VT *>(slot);
+        const T *s = reinterpret_cast<const T *>(&v);
+#pragma unroll
+        for (int i = 0; i < V; ++i) r[i] = s[i];
+    } else {
+        const T x = *slot;
+#pragma unroll
+        for (int i = 0; i < V; ++i) r[i] = x;
+    }
 }
 
 }  // namespace bgl

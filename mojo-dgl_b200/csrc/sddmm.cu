@@ -67,8 +67,8 @@ __global__ void __launch_bounds__(256) k_sddmm(const SddmmArgs<T> a) {
             for (int64_t cv = t; cv < cvn; cv += ts) {
                 T l[V], r[V], o[V];
                 if (cv == t) {  // the lane's first columns: the common, one-vector case
-                    if (NEED_L) load_mapped<T, V>(a.lhs, li, lmap, l);
-                    if (NEED_R) load_mapped<T, V>(a.rhs, ri, rmap, r);
+                    if (NEED_L) load_mapped<T, V>(a.lhs, li, (int64_t)t * V, lmap, l);
+                    if (NEED_R) load_mapped<T, V>(a.rhs, ri, (int64_t)t * V, rmap, r);
                 } else {
                     if (NEED_L) load_cols<T, V>(a.lhs, li, cv * V, l);
                     if (NEED_R) load_cols<T, V>(a.rhs, ri, cv * V, r);

@@ -8,9 +8,16 @@ namespace {
 template <typename T, int OP, int RED, int V, int J, bool ACC>
 int launch_kernels(const SpmmArgs<T> &a, cudaStream_t s) {
     int64_t threads = a.num_chunks * a.num_slices * a.ts;
-    int grid = (int)((threads + 255) / 256);
+    int grid = (int)((threads + kSpmmBlock - 1) / kSpmmBlock);
     if (grid < 1) grid = 1;
-    k_spmm<T, OP, RED, V, J, ACC><<<grid, 256, 0, s>>>(a);
+    // the gather ring lives in dynamic shared memory (64 KB per block for
+    // 16-byte slots), above the 48 KB a launch gets without opting in
+    constexpr int smem = Stages<T, OP, V>::smem;
+    auto k = k_spmm<T, OP, RED, V, J, ACC>;
+    BGL_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    BGL_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                  cudaSharedmemCarveoutMaxShared));
+    k<<<grid, kSpmmBlock, smem, s>>>(a);
     BGL_LAUNCH_CHECK();
     int fgrid = (int)((a.num_chunks * a.ts + 255) / 256);
     if (fgrid < 1) fgrid = 1;

@@ -102,7 +102,7 @@ __device__ __forceinline__ void fold(T &acc, int32_t &pos, T m, int32_t p) {
     } else if (RED == BGL_RED_MIN) {
         if (m < acc) { acc = m; pos = p; }
     } else {
-        acc = Arith<T>::add(acc, m);
+            acc = Arith<T>::add(acc, m);
     }
 }
 
@@ -111,64 +111,91 @@ __device__ __forceinline__ void fold(T &acc, int32_t &pos, T m, int32_t p) {
 // mode the row is first folded into what `out` already holds (a partial result
 // over other edges of the same rows): sums add, max/min keep the better value,
 // and on a tie the smaller edge id -- the earlier message in CSR order -- wins.
+// `row_len` is the row's CSR length when the caller already holds it (the
+// main pass does), else -1.
 template <typename T, int RED, int V, int J, bool ACC>
 __device__ __forceinline__ void emit_row(const SpmmArgs<T> &a, int64_t row, int64_t cb, int t,
                                          int64_t cvn, const T (&acc)[J][V],
-                                         const int32_t (&pos)[J][V]) {
+                                         const int32_t (&pos)[J][V], int64_t row_len) {
     T scale = T(1);
     if (a.mean) {
-        int64_t dg = a.deg ? a.deg[row] : a.indptr[row + 1] - a.indptr[row];
+        int64_t dg = a.deg                ? a.deg[row]
+                     : row_len >= 0 ? row_len
+                                    : a.indptr[row + 1] - a.indptr[row];
         scale = dg < 1 ? T(1) : T(dg);
     }
     constexpr bool ARG = RED == BGL_RED_MAX || RED == BGL_RED_MIN;
+    if constexpr (!ACC) {
 #pragma unroll
-    for (int j = 0; j < J; ++j) {
-        int64_t cv = cb + t + (int64_t)j * a.ts;
-        if (cv >= cvn) continue;
-        int64_t off = row * a.dout + cv * V;
-        T o[V];
-        int64_t ae[V], au[V];
-        bool take[V];
-#pragma unroll
-        for (int i = 0; i < V; ++i) {
-            const int32_t p = pos[j][i];
-            ae[i] = p < 0 ? -1 : (a.eid ? (int64_t)a.eid[p] : (int64_t)p);
-            au[i] = (ARG && a.arg_u && p >= 0) ? (int64_t)a.indices[p] : -1;
-            take[i] = true;
-        }
-        if (ACC) {
-            T old[V];
-            load_vec<T, V>(a.out + off, old);
+        for (int j = 0; j < J; ++j) {
+            int64_t cv = cb + t + (int64_t)j * a.ts;
+            if (cv >= cvn) continue;
+            int64_t off = row * a.dout + cv * V;
+            T o[V];
 #pragma unroll
             for (int i = 0; i < V; ++i) {
-                if (ARG) {
-                    const int64_t oe = a.arg_e ? a.arg_e[off + i] : -1;
-                    const T v = acc[j][i];
-                    const bool better = RED == BGL_RED_MAX ? v > old[i] : v < old[i];
-                    take[i] = better || (v == old[i] && ae[i] >= 0 && (oe < 0 || ae[i] < oe));
-                    o[i] = take[i] ? v : old[i];
-                } else {
-                    o[i] = Arith<T>::add(old[i], acc[j][i]);
+                T v = acc[j][i];
+                if (a.mean) v = Arith<T>::div(v, scale);
+                if (a.zero_inf && isinf(v)) v = T(0);
+                o[i] = v;
+            }
+            store_vec<T, V>(a.out + off, o);
+            if (ARG) {
+#pragma unroll
+                for (int i = 0; i < V; ++i) {
+                    int32_t p = pos[j][i];
+                    if (a.arg_u) a.arg_u[off + i] = p < 0 ? -1 : (int64_t)a.indices[p];
+                    if (a.arg_e) a.arg_e[off + i] = p < 0 ? -1 : (a.eid ? (int64_t)a.eid[p] : (int64_t)p);
                 }
             }
-        } else {
-#pragma unroll
-            for (int i = 0; i < V; ++i) o[i] = acc[j][i];
         }
+    } else {
 #pragma unroll
-        for (int i = 0; i < V; ++i) {
-            T v = o[i];
-            if (a.mean) v = Arith<T>::div(v, scale);
-            if (a.zero_inf && isinf(v)) v = T(0);
-            o[i] = v;
-        }
-        store_vec<T, V>(a.out + off, o);
-        if (ARG) {
+        for (int j = 0; j < J; ++j) {
+            int64_t cv = cb + t + (int64_t)j * a.ts;
+            if (cv >= cvn) continue;
+            int64_t off = row * a.dout + cv * V;
+            T o[V];
+            int64_t ae[V], au[V];
+            bool take[V];
 #pragma unroll
             for (int i = 0; i < V; ++i) {
-                if (!take[i]) continue;
-                if (a.arg_u) a.arg_u[off + i] = au[i];
-                if (a.arg_e) a.arg_e[off + i] = ae[i];
+                const int32_t p = pos[j][i];
+                ae[i] = p < 0 ? -1 : (a.eid ? (int64_t)a.eid[p] : (int64_t)p);
+                au[i] = (ARG && a.arg_u && p >= 0) ? (int64_t)a.indices[p] : -1;
+                take[i] = true;
+            }
+            {
+                T old[V];
+                load_vec<T, V>(a.out + off, old);
+#pragma unroll
+                for (int i = 0; i < V; ++i) {
+                    if (ARG) {
+                        const int64_t oe = a.arg_e ? a.arg_e[off + i] : -1;
+                        const T v = acc[j][i];
+                        const bool better = RED == BGL_RED_MAX ? v > old[i] : v < old[i];
+                        take[i] = better || (v == old[i] && ae[i] >= 0 && (oe < 0 || ae[i] < oe));
+                        o[i] = take[i] ? v : old[i];
+                    } else {
+                        o[i] = Arith<T>::add(old[i], acc[j][i]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+                T v = o[i];
+                if (a.mean) v = Arith<T>::div(v, scale);
+                if (a.zero_inf && isinf(v)) v = T(0);
+                o[i] = v;
+            }
+            store_vec<T, V>(a.out + off, o);
+            if (ARG) {
+#pragma unroll
+                for (int i = 0; i < V; ++i) {
+                    if (!take[i]) continue;
+                    if (a.arg_u) a.arg_u[off + i] = au[i];
+                    if (a.arg_e) a.arg_e[off + i] = ae[i];
+                }
             }
         }
     }
@@ -191,45 +218,63 @@ __device__ __forceinline__ void store_piece(const SpmmArgs<T> &a, T *val, int32_
     }
 }
 
-// Edges a lane keeps in flight: about eight vector loads per lane whatever
-// the row width, halved when both operands are gathered.
-// Measured on config 3 (125M edges, 128 fp32 columns): 4 edges in flight per
-// lane with 4 resident 256-thread blocks per SM (64 registers) ran copy_u sum
-// in 10.0 ms and max in 14.9 ms; 8 edges with 3 blocks: 10.0 / 22.2 ms; 8 with
-// 2 blocks: 11.2 / 31.7 ms -- occupancy beats per-lane depth once the walk
-// streams across row ends.
+// The gather pipeline.  A team walks its chunk's edges in groups of UN; the
+// rows of the next P groups are already being copied into the lane's shared
+// slots (cp.async) while the current group is folded, so each lane keeps
+// P * UN rows in flight without holding them in registers.  A ring of
+// P + 1 stages lets the copy for group g + P go into the stage that group g - 1
+// was folded from, whose values the fold has already consumed.
 #ifndef BGL_SPMM_UN
-#define BGL_SPMM_UN 4  // edges in flight per lane for rows of <= 32 vectors
+#define BGL_SPMM_UN 4  // edges per group, copy ops (one gathered row per edge)
 #endif
-#ifndef BGL_SPMM_MINB
-#define BGL_SPMM_MINB 4  // resident 256-thread blocks per SM the registers must allow
-#endif
-// Ops that gather two rows per edge (u_op_e) keep their own depth and
-// occupancy: twice the loads per edge, twice the registers per edge.
 #ifndef BGL_SPMM_UN_BIN
-#define BGL_SPMM_UN_BIN 2
+#define BGL_SPMM_UN_BIN 2  // edges per group when both operands are gathered
 #endif
-#ifndef BGL_SPMM_MINB_BIN
-#define BGL_SPMM_MINB_BIN 4
+#ifndef BGL_SPMM_DEPTH
+#define BGL_SPMM_DEPTH 3  // groups in flight ahead of the one being folded
 #endif
-template <int OP, int J>
-struct InFlight {
+#ifndef BGL_SPMM_DEPTH_BIN
+#define BGL_SPMM_DEPTH_BIN 3
+#endif
+constexpr int kSpmmBlock = 256;
+constexpr int kSmemPerSm = 228 * 1024;  // shared memory per SM, 1 KB of it reserved per block
+
+template <typename T, int OP, int V>
+struct Stages {
     static constexpr bool both = OP != BGL_OP_COPY_LHS && OP != BGL_OP_COPY_RHS;
-    static constexpr int value = both ? BGL_SPMM_UN_BIN : BGL_SPMM_UN;
-    static constexpr int minb = both ? BGL_SPMM_MINB_BIN : BGL_SPMM_MINB;
+    static constexpr int un = both ? BGL_SPMM_UN_BIN : BGL_SPMM_UN;
+    static constexpr int depth = both ? BGL_SPMM_DEPTH_BIN : BGL_SPMM_DEPTH;
+    static constexpr int ring = depth + 1;
+    static constexpr int nops = both ? 2 : 1;
+    static constexpr int slot = V * (int)sizeof(T);  // bytes per lane per operand row
+    static constexpr int smem = ring * un * nops * kSpmmBlock * slot;
+    // resident blocks the ring allows, at most three (85 registers a thread)
+    static constexpr int fit = kSmemPerSm / (smem + 1024);
+    static constexpr int minb = fit < 1 ? 1 : fit > 3 ? 3 : fit;
+    static_assert(smem <= 227 * 1024, "gather ring larger than a block's shared memory");
 };
 
 // The main pass.  A team walks its chunk's edge range [c0.y, c1.y) in full
 // groups of UN edges regardless of where rows end -- a group can close one
-// row and open the next -- so each lane always has UN row loads in flight,
-// and the next group's neighbour ids are fetched while the current group's
-// rows are still arriving.  Row ends are handled as the group is folded, in
-// CSR order, so the arithmetic is exactly the per-row sequential fold.
+// row and open the next -- so the copy pipeline never drains at a row end.
+// Row ends are handled as the group is folded, in CSR order, so the
+// arithmetic is exactly the per-row sequential fold.
 template <typename T, int OP, int RED, int V, int J, bool ACC>
-__global__ void __launch_bounds__(256, (InFlight<OP, J>::minb)) k_spmm(const SpmmArgs<T> a) {
-    constexpr int UN = InFlight<OP, J>::value;
+__global__ void __launch_bounds__(kSpmmBlock, (Stages<T, OP, V>::minb)) k_spmm(const SpmmArgs<T> a) {
+    static_assert(J == 1, "the staged gather keeps one column vector per lane");
+    using S = Stages<T, OP, V>;
+    constexpr int UN = S::un, P = S::depth, R = S::ring;
     constexpr bool NEED_L = OP != BGL_OP_COPY_RHS;
     constexpr bool NEED_R = OP != BGL_OP_COPY_LHS;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    // slot (stage, u, operand) of this thread: lanes of a warp are adjacent,
+    // so the copies and the read-backs are conflict-free
+    const uint32_t sbase = smem_addr(smem_raw) + threadIdx.x * S::slot;
+    const T *pbase = reinterpret_cast<const T *>(smem_raw + threadIdx.x * S::slot);
+    auto slot_off = [](int stage, int u, int op) {
+        return ((stage * UN + u) * S::nops + op) * kSpmmBlock * S::slot;
+    };
+
     const int ts = a.ts;
     const int t = threadIdx.x & (ts - 1);
     const int64_t team = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) / ts;
@@ -247,26 +292,27 @@ __global__ void __launch_bounds__(256, (InFlight<OP, J>::minb)) k_spmm(const Spm
     const int64_t *__restrict__ indptr = a.indptr;
 
     int32_t head_row = -1, tail_row = -1;
-    for (int32_t cb = slice * ts * J; cb < cvn; cb += a.num_slices * ts * J) {
+    for (int32_t cb = slice * ts; cb < cvn; cb += a.num_slices * ts) {
         int32_t x = x0;
         if (x >= nrows) break;  // an empty trailing chunk
+        const int32_t cv = cb + t;  // this lane's column vector (may be past the row)
+        const bool live = cv < cvn;
+        const int64_t k0 = (int64_t)cv * V;
         int32_t rs = (int32_t)indptr[x];
         int32_t re = (x < x1) ? (int32_t)indptr[x + 1] : ye;
         int32_t row_begin = y0;  // first edge of the current row in this chunk
         T acc[J][V];
         int32_t pos[J][V];
 #pragma unroll
-        for (int j = 0; j < J; ++j)
-#pragma unroll
-            for (int i = 0; i < V; ++i) {
-                acc[j][i] = identity<RED, T>();
-                pos[j][i] = -1;
-            }
+        for (int i = 0; i < V; ++i) {
+            acc[0][i] = identity<RED, T>();
+            pos[0][i] = -1;
+        }
         // closes row x (emitted, or stored as a head piece if it began in an
         // earlier chunk) and opens row x + 1
         auto close_row = [&]() {
             if (row_begin == rs) {
-                emit_row<T, RED, V, J, ACC>(a, x, cb, t, cvn, acc, pos);
+                emit_row<T, RED, V, J, ACC>(a, x, cb, t, cvn, acc, pos, re - rs);
             } else {
                 store_piece<T, RED, V, J>(a, a.head_val, a.head_pos, chunk, cb, t, cvn, acc, pos);
                 head_row = x;
@@ -276,72 +322,78 @@ __global__ void __launch_bounds__(256, (InFlight<OP, J>::minb)) k_spmm(const Spm
             ++x;
             re = (x < x1) ? (int32_t)indptr[x + 1] : ye;
 #pragma unroll
-            for (int j = 0; j < J; ++j)
-#pragma unroll
-                for (int i = 0; i < V; ++i) {
-                    acc[j][i] = identity<RED, T>();
-                    pos[j][i] = -1;
-                }
+            for (int i = 0; i < V; ++i) {
+                acc[0][i] = identity<RED, T>();
+                pos[0][i] = -1;
+            }
         };
 
-        // this lane's columns in each operand, fixed for the whole walk (J = 1)
-        ColMap<V> lmap[J], rmap[J];
-#pragma unroll
-        for (int j = 0; j < J; ++j) {
-            const int64_t k0 = (int64_t)(cb + t + j * ts) * V;
-            if (NEED_L) lmap[j] = col_map<T, V>(a.lhs, k0);
-            if (NEED_R) rmap[j] = col_map<T, V>(a.rhs, k0);
-        }
+        // a broadcast operand's columns are fixed for the walk
+        ColMap<V> lmap, rmap;
+        if (NEED_L) lmap = col_map<T, V>(a.lhs, k0);
+        if (NEED_R) rmap = col_map<T, V>(a.rhs, k0);
+
+        // ids of the next group to copy, fetched one group ahead of its copy
         int32_t src[UN], edg[UN];
-        auto fetch_ids = [&](int32_t e0, int32_t(&s)[UN], int32_t(&d)[UN]) {
+        int32_t e_copy = y0;
+        auto fetch_ids = [&]() {
 #pragma unroll
             for (int u = 0; u < UN; ++u) {
-                if (e0 + u < ye) {
-                    if (NEED_L) s[u] = __ldg(a.indices + e0 + u);
-                    if (NEED_R) d[u] = a.eid ? __ldg(a.eid + e0 + u) : e0 + u;
+                if (e_copy + u < ye) {
+                    if (NEED_L) src[u] = __ldg(a.indices + e_copy + u);
+                    if (NEED_R) edg[u] = a.eid ? __ldg(a.eid + e_copy + u) : e_copy + u;
                 }
             }
         };
-        fetch_ids(y0, src, edg);
-        for (int32_t e0 = y0; e0 < ye; e0 += UN) {
-            const int n = (ye - e0) < UN ? (ye - e0) : UN;
-            T lv[UN][J][V], rv[UN][J][V];
+        auto copy_group = [&](int stage) {
+            if (live) {
 #pragma unroll
-            for (int u = 0; u < UN; ++u) {
-                if (u < n) {
-#pragma unroll
-                    for (int j = 0; j < J; ++j) {
-                        const int32_t cv = cb + t + j * ts;
-                        if (cv < cvn) {
-                            if (NEED_L) load_mapped<T, V>(a.lhs, src[u], lmap[j], lv[u][j]);
-                            if (NEED_R) load_mapped<T, V>(a.rhs, edg[u], rmap[j], rv[u][j]);
-                        }
+                for (int u = 0; u < UN; ++u) {
+                    if (e_copy + u < ye) {
+                        if (NEED_L)
+                            stage_cols<T, V>(a.lhs, src[u], k0, lmap, sbase + slot_off(stage, u, 0));
+                        if (NEED_R)
+                            stage_cols<T, V>(a.rhs, edg[u], k0, rmap,
+                                             sbase + slot_off(stage, u, S::nops - 1));
                     }
                 }
             }
-            int32_t nsrc[UN], nedg[UN];
-            fetch_ids(e0 + UN, nsrc, nedg);
+            cp_async_commit();  // an empty group past the chunk end keeps the count
+            e_copy += UN;
+            fetch_ids();
+        };
+        fetch_ids();
+#pragma unroll
+        for (int g = 0; g < P; ++g) copy_group(g);
+        int fold_stage = 0, copy_stage = P;
+        for (int32_t e0 = y0; e0 < ye; e0 += UN) {
+            copy_group(copy_stage);
+            cp_async_wait<P>();  // the group at e0 has landed
+            const int n = (ye - e0) < UN ? (ye - e0) : UN;
 #pragma unroll
             for (int u = 0; u < UN; ++u) {
                 if (u < n) {
                     const int32_t e = e0 + u;
                     while (e >= re) close_row();
+                    T lv[V], rv[V];
 #pragma unroll
-                    for (int j = 0; j < J; ++j)
+                    for (int i = 0; i < V; ++i) lv[i] = rv[i] = T(0);
+                    if (live) {
+                        if (NEED_L) read_cols<T, V>(a.lhs, pbase + slot_off(fold_stage, u, 0) / sizeof(T), lv);
+                        if (NEED_R)
+                            read_cols<T, V>(a.rhs, pbase + slot_off(fold_stage, u, S::nops - 1) / sizeof(T), rv);
+                    }
 #pragma unroll
-                        for (int i = 0; i < V; ++i) {
-                            T m = message<OP, T>(NEED_L ? lv[u][j][i] : T(0),
-                                                 NEED_R ? rv[u][j][i] : T(0));
-                            fold<RED, T>(acc[j][i], pos[j][i], m, e);
-                        }
+                    for (int i = 0; i < V; ++i) {
+                        T m = message<OP, T>(NEED_L ? lv[i] : T(0), NEED_R ? rv[i] : T(0));
+                        fold<RED, T>(acc[0][i], pos[0][i], m, e);
+                    }
                 }
             }
-#pragma unroll
-            for (int u = 0; u < UN; ++u) {
-                src[u] = nsrc[u];
-                edg[u] = nedg[u];
-            }
+            fold_stage = fold_stage + 1 == R ? 0 : fold_stage + 1;
+            copy_stage = copy_stage + 1 == R ? 0 : copy_stage + 1;
         }
+        cp_async_wait<0>();
         while (x < x1) close_row();  // rows ending at the chunk end, empty rows
         if (x < nrows && ye > row_begin) {
             // row x continues into the next chunk: its first (or middle) piece
@@ -394,7 +446,7 @@ __global__ void __launch_bounds__(256) k_spmm_fixup(const SpmmArgs<T> a) {
                 }
             }
         }
-        emit_row<T, RED, V, J, ACC>(a, row, cb, t, cvn, acc, pos);
+        emit_row<T, RED, V, J, ACC>(a, row, cb, t, cvn, acc, pos, -1);
     }
 }
 
