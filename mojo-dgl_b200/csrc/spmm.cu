@@ -115,7 +115,6 @@ static int run_spmm(const int64_t *indptr, const int32_t *indices, const int32_t
     a.dout = dout;
     a.arg_u = (red == BGL_RED_MAX || red == BGL_RED_MIN) ? arg_u : nullptr;
     a.arg_e = (red == BGL_RED_MAX || red == BGL_RED_MIN) ? arg_e : nullptr;
-    a.mean = red == BGL_RED_MEAN;
     a.zero_inf = (flags & BGL_ZERO_INF) != 0;
     a.accumulate = (flags & BGL_ACCUMULATE) != 0;
     a.ts = p.ts;

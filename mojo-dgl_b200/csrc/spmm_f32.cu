@@ -35,8 +35,8 @@ int launch_one(const SpmmArgs<T> &a, cudaStream_t s) {
 template <typename T, int OP, int V, int J>
 int by_reduce(const SpmmArgs<T> &a, int red, cudaStream_t s) {
     switch (red) {
-    case BGL_RED_SUM:
-    case BGL_RED_MEAN: return launch_one<T, OP, BGL_RED_SUM, V, J>(a, s);
+    case BGL_RED_SUM: return launch_one<T, OP, BGL_RED_SUM, V, J>(a, s);
+    case BGL_RED_MEAN: return launch_one<T, OP, BGL_RED_MEAN, V, J>(a, s);
     case BGL_RED_MAX: return launch_one<T, OP, BGL_RED_MAX, V, J>(a, s);
     case BGL_RED_MIN: return launch_one<T, OP, BGL_RED_MIN, V, J>(a, s);
     }

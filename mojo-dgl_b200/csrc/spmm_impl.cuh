@@ -40,7 +40,6 @@ struct SpmmArgs {
     int64_t dout;
     int64_t *arg_u;
     int64_t *arg_e;
-    bool mean;
     bool zero_inf;
     bool accumulate;  // BGL_ACCUMULATE: selects the kernels compiled with ACC = true
     int ts;  // lanes per team (power of two <= 32)
@@ -118,7 +117,8 @@ __device__ __forceinline__ void emit_row(const SpmmArgs<T> &a, int64_t row, int6
                                          int64_t cvn, const T (&acc)[J][V],
                                          const int32_t (&pos)[J][V], int64_t row_len) {
     T scale = T(1);
-    if (a.mean) {
+    constexpr bool MEAN = RED == BGL_RED_MEAN;  // a sum divided by the in-degree
+    if (MEAN) {
         int64_t dg = a.deg                ? a.deg[row]
                      : row_len >= 0 ? row_len
                                     : a.indptr[row + 1] - a.indptr[row];
@@ -135,7 +135,7 @@ __device__ __forceinline__ void emit_row(const SpmmArgs<T> &a, int64_t row, int6
 #pragma unroll
             for (int i = 0; i < V; ++i) {
                 T v = acc[j][i];
-                if (a.mean) v = Arith<T>::div(v, scale);
+                if (MEAN) v = Arith<T>::div(v, scale);
                 if (a.zero_inf && isinf(v)) v = T(0);
                 o[i] = v;
             }
@@ -184,7 +184,7 @@ __device__ __forceinline__ void emit_row(const SpmmArgs<T> &a, int64_t row, int6
 #pragma unroll
             for (int i = 0; i < V; ++i) {
                 T v = o[i];
-                if (a.mean) v = Arith<T>::div(v, scale);
+                if (MEAN) v = Arith<T>::div(v, scale);
                 if (a.zero_inf && isinf(v)) v = T(0);
                 o[i] = v;
             }
@@ -228,14 +228,19 @@ __device__ __forceinline__ void store_piece(const SpmmArgs<T> &a, T *val, int32_
 #define BGL_SPMM_UN 4  // edges per group, copy ops (one gathered row per edge)
 #endif
 #ifndef BGL_SPMM_UN_BIN
-#define BGL_SPMM_UN_BIN 2  // edges per group when both operands are gathered
+#define BGL_SPMM_UN_BIN 1  // edges per group when both operands are gathered
 #endif
 #ifndef BGL_SPMM_DEPTH
 #define BGL_SPMM_DEPTH 3  // groups in flight ahead of the one being folded
 #endif
 #ifndef BGL_SPMM_DEPTH_BIN
-#define BGL_SPMM_DEPTH_BIN 3
+#define BGL_SPMM_DEPTH_BIN 4
 #endif
+// Measured on config 3 (125M edges, 128 fp32 columns) and config 2: copy ops
+// run best with groups of 4 and 3 in flight at three blocks per SM (copy_u sum
+// 9.5 ms; groups of 2 x 6, 3 x 4, 6 x 2, or any two-block ring: 10.2-10.9 ms);
+// binary ops with single-edge groups 4 deep (u_mul_e 19.5 ms on config 3,
+// 12.1 ms on config 2; 2 x 3: 21.1 / 14.0 ms).
 constexpr int kSpmmBlock = 256;
 constexpr int kSmemPerSm = 228 * 1024;  // shared memory per SM, 1 KB of it reserved per block
 

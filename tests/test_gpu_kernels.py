@@ -158,6 +158,35 @@ def test_split_rows_are_deterministic(small_chunks):
     np.testing.assert_array_equal(a, b)
 
 
+@pytest.mark.parametrize("split", [False, True])
+def test_float32_mean_is_the_correctly_rounded_sum_over_degree(split, request):
+    """copy_u_mean divides each row's float32 sum by its in-degree once, so it
+    must equal copy_u_sum's output divided by the degree in IEEE float32 bit
+    for bit -- degrees 0..4000 and a few hundred thousand, values from 2^-110
+    to 2^110, zeros, inf and NaN."""
+    if split:
+        request.getfixturevalue("small_chunks")
+    rng = np.random.default_rng(91)
+    deg = np.concatenate([np.arange(4001), rng.integers(4001, 300_000, 12),
+                          [65536, 65537, 131071]])
+    n = deg.size
+    v = np.repeat(np.arange(n), deg)
+    u = rng.integers(0, 2048, v.size)
+    x = rng.normal(size=(n, 64)) * np.exp2(rng.integers(-40, 41, size=(n, 1)))
+    x[:64] = rng.normal(size=(64, 64)) * 2.0 ** -110
+    x[64:128] = rng.normal(size=(64, 64)) * 2.0 ** 110
+    x[128, :8] = 0.0
+    x[129, 8] = np.inf
+    x[130, 9] = np.nan
+    x = x.astype(np.float32)
+    g = dgl.graph((u, v), num_nodes=n)
+    s = ops.copy_u_sum(g, x)
+    m = ops.copy_u_mean(g, x)
+    want = s / np.maximum(deg, 1).astype(np.float32)[:, None]
+    assert want.dtype == np.float32
+    np.testing.assert_array_equal(m, want)
+
+
 def test_head_broadcast_gat_layer(orc):
     """BASELINE config 2's pipeline at a small size: u_add_v on (N, H, 1),
     leaky_relu, edge_softmax over (E, H, 1), u_mul_e_sum of (N, H, D) by
