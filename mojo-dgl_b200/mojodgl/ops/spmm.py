@@ -63,7 +63,9 @@ def _run(g, op, reduce_op, lhs_data, rhs_data, with_arg=False, zero_inf=False, c
         lt, lw, ldiv, rt, rw, rdiv = b.lhs, b.lw, b.ldiv, b.rhs, b.rw, b.rdiv
         code = BINARY_OPS[op]
 
-    indptr, indices, eid, deg = csr if csr is not None else g._device().in_csr
+    # the in-CSR holds every in-edge, so the mean divides by the row length,
+    # which the kernel has in hand: no degree array is passed
+    indptr, indices, eid, _ = csr if csr is not None else g._device().in_csr
     red = REDUCERS[reduce_op]
     dev = T.device()
     out = torch.empty((num_dst, dout), dtype=dtype, device=dev)
@@ -73,7 +75,7 @@ def _run(g, op, reduce_op, lhs_data, rhs_data, with_arg=False, zero_inf=False, c
         arg_e = torch.empty((num_dst, dout), dtype=torch.int64, device=dev) if code != OP_COPY_LHS else None
     nbytes = lib().bgl_gspmm_workspace_size(num_dst, num_edges, dout, T.code_of(dtype), red)
     ws = T.workspace(nbytes)
-    rc = lib().bgl_gspmm(T.ptr(indptr), T.ptr(indices), T.ptr(eid), T.ptr(deg), num_dst, num_edges,
+    rc = lib().bgl_gspmm(T.ptr(indptr), T.ptr(indices), T.ptr(eid), None, num_dst, num_edges,
                          T.ptr(lt), lw, ldiv, T.ptr(rt), rw, rdiv, T.ptr(out), dout, T.ptr(arg_u),
                          T.ptr(arg_e), T.code_of(dtype), code, red,
                          BGL_ZERO_INF if zero_inf else 0, T.ptr(ws), nbytes, T.stream())

@@ -113,7 +113,9 @@ class DeviceShard:
         nbytes = lib().bgl_gspmm_workspace_size(n, ne, d, code, red)
         if workspace is None or workspace.numel() < nbytes:
             workspace = T.workspace(nbytes)
-        check(lib().bgl_gspmm(T.ptr(self.indptr), T.ptr(self.indices), None, T.ptr(self.deg), n, ne,
+        # the shard holds every in-edge of its rows, so the mean's degree is
+        # the CSR row length, which the kernel has in hand (deg = NULL)
+        check(lib().bgl_gspmm(T.ptr(self.indptr), T.ptr(self.indices), None, None, n, ne,
                               T.ptr(feat), d, 1, None, 1, 1, T.ptr(out), d, T.ptr(arg_u), None, code,
                               OP_COPY_LHS, red, BGL_ZERO_INF if reduce_op in ("max", "min") else 0,
                               T.ptr(workspace), nbytes, T.stream()), "gspmm")
