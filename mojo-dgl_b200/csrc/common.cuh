@@ -250,38 +250,71 @@ __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// Starts the copy of the lane's V output columns [k0, k0 + V) of operand row
-// `row` into shared slot `dst` (V * sizeof(T) bytes, aligned to that size).
-// A uniform broadcast copies its one element; a non-uniform one copies each.
+// One operand as a lane reads it during a walk: the address of the lane's
+// first value in row 0 and the row stride in bytes, so a row's address is one
+// 32 x 32 -> 64-bit multiply-add.  `mode` 0: the lane's V values are adjacent
+// (a full operand, or any operand read one column at a time); 1: one value
+// serves all V columns (uniform broadcast); 2: each of the V values has its
+// own broadcast column (a divisor that V does not divide).
 template <typename T, int V>
-__device__ __forceinline__ void stage_cols(const Operand<T> &o, int64_t row, int64_t k0,
-                                           const ColMap<V> &m, uint32_t dst) {
-    const T *base = o.ptr + row * o.width;
+struct LaneCols {
+    const char *base;
+    uint32_t row_bytes;
+    int32_t mode;
+    int32_t k0;
+};
+
+template <typename T, int V>
+__device__ __forceinline__ LaneCols<T, V> lane_cols(const Operand<T> &o, int64_t k0) {
+    LaneCols<T, V> c;
+    c.row_bytes = (uint32_t)(o.width * (int64_t)sizeof(T));
+    c.k0 = (int32_t)k0;
     if (o.full) {
-        cp_async<V * sizeof(T)>(dst, base + k0);
+        c.mode = 0;
+        c.base = reinterpret_cast<const char *>(o.ptr + k0);
     } else if (o.uniform) {
-        cp_async<sizeof(T)>(dst, base + m.off);
+        c.mode = 1;
+        c.base = reinterpret_cast<const char *>(
+            o.ptr + ((uint32_t)k0 / (uint32_t)o.div) % (uint32_t)o.width);
     } else {
+        c.mode = 2;
+        c.base = reinterpret_cast<const char *>(o.ptr);
+    }
+    return c;
+}
+
+// Starts the copy of the lane's values of operand row `row` into shared slot
+// `dst` (V * sizeof(T) bytes, aligned to that size).
+template <typename T, int V>
+__device__ __forceinline__ void stage_row(const LaneCols<T, V> &c, const Operand<T> &o,
+                                          int32_t row, uint32_t dst) {
+    const char *src = c.base + (uint64_t)(uint32_t)row * c.row_bytes;
+    if (c.mode == 0) {
+        cp_async<V * sizeof(T)>(dst, src);
+    } else if (c.mode == 1) {
+        cp_async<sizeof(T)>(dst, src);
+    } else {
+        const T *r = reinterpret_cast<const T *>(src);
 #pragma unroll
         for (int i = 0; i < V; ++i)
             cp_async<sizeof(T)>(dst + i * sizeof(T),
-                                base + ((uint32_t)(m.off + i) / (uint32_t)o.div) % (uint32_t)o.width);
+                                r + ((uint32_t)(c.k0 + i) / (uint32_t)o.div) % (uint32_t)o.width);
     }
 }
 
-// Reads back what stage_cols copied into `slot`.
+// Reads back what stage_row copied into `slot`.
 template <typename T, int V>
-__device__ __forceinline__ void read_cols(const Operand<T> &o, const T *slot, T (&r)[V]) {
-    if (o.full || !o.uniform) {
+__device__ __forceinline__ void read_row(const LaneCols<T, V> &c, const T *slot, T (&r)[V]) {
+    if (c.mode == 1) {
+        const T x = *slot;
+#pragma unroll
+        for (int i = 0; i < V; ++i) r[i] = x;
+    } else {
         using VT = typename VecT<T, V>::type;
         const VT v = *reinterpret_cast<const VT *>(slot);
         const T *s = reinterpret_cast<const T *>(&v);
 #pragma unroll
         for (int i = 0; i < V; ++i) r[i] = s[i];
-    } else {
-        const T x = *slot;
-#pragma unroll
-        for (int i = 0; i < V; ++i) r[i] = x;
     }
 }
 

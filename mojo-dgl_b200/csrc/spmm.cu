@@ -166,6 +166,12 @@ int bgl_gspmm(const int64_t *indptr, const int32_t *indices, const int32_t *eid,
     if (num_rows >= (int64_t(1) << 31) || num_edges >= (int64_t(1) << 31))
         return fail(BGL_E_UNSUPPORTED, "bgl_gspmm: more than 2^31-1 rows or edges");
     const bool need_l = op != BGL_OP_COPY_RHS, need_r = op != BGL_OP_COPY_LHS;
+    // the kernels address a row's columns in 32 bits: row strides below 4 GiB,
+    // column indices and broadcast divisors below 2^31
+    const int64_t elem = dtype == BGL_F32 ? 4 : 8, lim = int64_t(1) << 31;
+    if (dout >= lim || (need_l && (lhs_width * elem >= 2 * lim || lhs_div >= lim)) ||
+        (need_r && (rhs_width * elem >= 2 * lim || rhs_div >= lim)))
+        return fail(BGL_E_UNSUPPORTED, "bgl_gspmm: a feature row of 4 GiB or more");
     if (need_l && (lhs_width < 1 || lhs_div < 1))
         return fail(BGL_E_INVALID, "bgl_gspmm: lhs width/div must be >= 1");
     if (need_r && (rhs_width < 1 || rhs_div < 1))

@@ -333,39 +333,60 @@ __global__ void __launch_bounds__(kSpmmBlock, (Stages<T, OP, V>::minb)) k_spmm(c
             }
         };
 
-        // a broadcast operand's columns are fixed for the walk
-        ColMap<V> lmap, rmap;
-        if (NEED_L) lmap = col_map<T, V>(a.lhs, k0);
-        if (NEED_R) rmap = col_map<T, V>(a.rhs, k0);
+        // the lane's columns of each operand, fixed for the walk
+        LaneCols<T, V> lc, rc;
+        if (NEED_L) lc = lane_cols<T, V>(a.lhs, k0);
+        if (NEED_R) rc = lane_cols<T, V>(a.rhs, k0);
 
-        // ids of the next group to copy, fetched one group ahead of its copy
+        // ids of the next group to copy, fetched one group ahead of its copy;
+        // only a chunk's last group needs a bound on every edge
         int32_t src[UN], edg[UN];
         int32_t e_copy = y0;
+        auto fetch_one = [&](int u) {
+            if (NEED_L) src[u] = __ldg(a.indices + e_copy + u);
+            if (NEED_R) edg[u] = a.eid ? __ldg(a.eid + e_copy + u) : e_copy + u;
+        };
         auto fetch_ids = [&]() {
+            if (e_copy + UN <= ye) {
 #pragma unroll
-            for (int u = 0; u < UN; ++u) {
-                if (e_copy + u < ye) {
-                    if (NEED_L) src[u] = __ldg(a.indices + e_copy + u);
-                    if (NEED_R) edg[u] = a.eid ? __ldg(a.eid + e_copy + u) : e_copy + u;
-                }
+                for (int u = 0; u < UN; ++u) fetch_one(u);
+            } else {
+#pragma unroll
+                for (int u = 0; u < UN; ++u)
+                    if (e_copy + u < ye) fetch_one(u);
             }
         };
+        auto copy_one = [&](int stage, int u) {
+            if (NEED_L) stage_row<T, V>(lc, a.lhs, src[u], sbase + slot_off(stage, u, 0));
+            if (NEED_R) stage_row<T, V>(rc, a.rhs, edg[u], sbase + slot_off(stage, u, S::nops - 1));
+        };
         auto copy_group = [&](int stage) {
-            if (live) {
+            if (live) {  // a lane past the row's last column copies nothing
+                if (e_copy + UN <= ye) {
 #pragma unroll
-                for (int u = 0; u < UN; ++u) {
-                    if (e_copy + u < ye) {
-                        if (NEED_L)
-                            stage_cols<T, V>(a.lhs, src[u], k0, lmap, sbase + slot_off(stage, u, 0));
-                        if (NEED_R)
-                            stage_cols<T, V>(a.rhs, edg[u], k0, rmap,
-                                             sbase + slot_off(stage, u, S::nops - 1));
-                    }
+                    for (int u = 0; u < UN; ++u) copy_one(stage, u);
+                } else {
+#pragma unroll
+                    for (int u = 0; u < UN; ++u)
+                        if (e_copy + u < ye) copy_one(stage, u);
                 }
             }
             cp_async_commit();  // an empty group past the chunk end keeps the count
             e_copy += UN;
             fetch_ids();
+        };
+        // folds edge e from slot (stage, u); a lane past the row's last column
+        // folds whatever its slot holds and never stores it
+        auto fold_one = [&](int stage, int u, int32_t e) {
+            while (e >= re) close_row();
+            T lv[V], rv[V];
+            if (NEED_L) read_row<T, V>(lc, pbase + slot_off(stage, u, 0) / sizeof(T), lv);
+            if (NEED_R) read_row<T, V>(rc, pbase + slot_off(stage, u, S::nops - 1) / sizeof(T), rv);
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+                T m = message<OP, T>(NEED_L ? lv[i] : T(0), NEED_R ? rv[i] : T(0));
+                fold<RED, T>(acc[0][i], pos[0][i], m, e);
+            }
         };
         fetch_ids();
 #pragma unroll
@@ -374,26 +395,13 @@ __global__ void __launch_bounds__(kSpmmBlock, (Stages<T, OP, V>::minb)) k_spmm(c
         for (int32_t e0 = y0; e0 < ye; e0 += UN) {
             copy_group(copy_stage);
             cp_async_wait<P>();  // the group at e0 has landed
-            const int n = (ye - e0) < UN ? (ye - e0) : UN;
+            if (e0 + UN <= ye) {
 #pragma unroll
-            for (int u = 0; u < UN; ++u) {
-                if (u < n) {
-                    const int32_t e = e0 + u;
-                    while (e >= re) close_row();
-                    T lv[V], rv[V];
+                for (int u = 0; u < UN; ++u) fold_one(fold_stage, u, e0 + u);
+            } else {
 #pragma unroll
-                    for (int i = 0; i < V; ++i) lv[i] = rv[i] = T(0);
-                    if (live) {
-                        if (NEED_L) read_cols<T, V>(a.lhs, pbase + slot_off(fold_stage, u, 0) / sizeof(T), lv);
-                        if (NEED_R)
-                            read_cols<T, V>(a.rhs, pbase + slot_off(fold_stage, u, S::nops - 1) / sizeof(T), rv);
-                    }
-#pragma unroll
-                    for (int i = 0; i < V; ++i) {
-                        T m = message<OP, T>(NEED_L ? lv[i] : T(0), NEED_R ? rv[i] : T(0));
-                        fold<RED, T>(acc[0][i], pos[0][i], m, e);
-                    }
-                }
+                for (int u = 0; u < UN; ++u)
+                    if (e0 + u < ye) fold_one(fold_stage, u, e0 + u);
             }
             fold_stage = fold_stage + 1 == R ? 0 : fold_stage + 1;
             copy_stage = copy_stage + 1 == R ? 0 : copy_stage + 1;
