@@ -156,7 +156,8 @@ int bgl_gsddmm(const int32_t *u, const int32_t *v, int64_t num_edges, const void
  * with indptr[0] = 0 and indptr[num_rows] = num_items (the compat layer turns
  * the reference's clamped offsets, src/ported.mojo:694-699, into such a CSR).
  * Heavy rows are split over merge-path chunks; the workspace holds the chunk
- * boundaries and the split rows' per-column (max, sum) pieces. */
+ * boundaries, the split rows' per-column (max, sum) pieces, every row's
+ * (max, 1 / sum) and every item's row. */
 size_t bgl_softmax_workspace_size(int64_t num_rows, int64_t num_items, int64_t d, int dtype);
 int bgl_edge_softmax(const int64_t *indptr, const int32_t *eid, const int8_t *mask,
                      int64_t num_rows, int64_t num_items, const void *logits, void *out,

@@ -7,29 +7,34 @@
 // edge_softmax reaches the items through the CSR's edge ids; segment_softmax's
 // items are the consecutive rows of `value` (eid = identity).
 //
-// Work split: the gSpMM engine's merge path over (row ends, items), so a team
-// of lanes gets the same number of items whatever the degrees are -- a
-// 50,000-edge attention hub is spread over many teams.  Lanes own V adjacent
-// columns; a team streams its chunk's items in groups of UN across row ends and
-// folds, per column, an online (max, sum of exp(z - max)) pair: a larger z
-// rescales the running sum by exp(old max - z).  A row that closes inside the
-// chunk stores its (max, sum) in a per-row buffer; a row split over chunks
-// leaves one (max, sum) piece per chunk and the fixup kernel folds the pieces
-// in CSR order into the row's entry.  The write pass then streams the same
-// chunks again and writes exp(z - max) / sum, reloading the stats only when
-// it crosses a row end -- no team ever runs a per-row loop the other teams of
-// its warp would have to wait for.
-// The online sum rounds differently from the reference's max-then-sum passes
-// (and CUDA's exp is not the Mojo stdlib's), so results are compared with a
-// relative tolerance (1e-12 in float64).
+// Pass 1 (k_softmax_stats): one warp per merge-path chunk of (row ends, items),
+// so a warp gets the same number of items whatever the degrees are and a
+// 50,000-edge attention hub is spread over many warps.  The warp's lanes are
+// split into W = 32 / CV items x CV column vectors: with 8 float32 columns a
+// step covers 16 items, with 128 or more one item (column blocks of 32 vectors
+// loop).  A step finds each item's row among 32 row ends held across the warp
+// (a binary search over shuffles), reduces every row's items of the step with
+// segmented warp scans -- max, broadcast, exp(z - max), sum -- and folds the
+// row left open at the end of the step into the next step.  A finished row
+// stores its (max, 1 / sum); a row split over chunks leaves a (max, sum) piece
+// per chunk, folded in CSR order by k_softmax_fixup.  The logits reach shared
+// memory through a per-lane cp.async ring several steps ahead of the fold, and
+// the pass records every item's row.
+// Pass 2 (k_softmax_apply): item-parallel, out = exp(z - max) * (1 / sum) with
+// the row the first pass recorded -- no walk, no divergence.
+// The rounding differs from the reference's max-then-sum loops (a tree of
+// partial sums, a multiply by the reciprocal, CUDA's exp), so results are
+// compared with a relative tolerance (1e-12 in float64).
 #include "spmm_impl.cuh"
-
-#ifndef BGL_SOFTMAX_MINB
-#define BGL_SOFTMAX_MINB 1  // resident 256-thread blocks per SM the registers must allow
-#endif
 
 namespace bgl {
 namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+constexpr int kSoftBlock = 256;
+#ifndef BGL_SOFTMAX_DEPTH
+#define BGL_SOFTMAX_DEPTH 4  // steps whose logits are in flight ahead of the fold
+#endif
 
 template <typename T>
 struct SoftArgs {
@@ -41,25 +46,17 @@ struct SoftArgs {
     const T *logits;
     T *out;
     int32_t d;
-    int32_t ts;
     int64_t num_chunks;
     const Coord *coords;
     int32_t *head_row;
     int32_t *tail_row;
-    T *head_m, *head_s, *tail_m, *tail_s;  // per chunk x d: the split rows' pieces
-    T *row_m, *row_s;                      // per row x d: each row's final (max, sum)
+    T *head_m, *head_s, *tail_m, *tail_s;  // per chunk x d: the split rows' (max, sum) pieces
+    T *row_m, *row_r;                      // per row x d: each row's max and 1 / sum
+    int32_t *item_row;                     // per item: its row
 };
 
-template <typename T>
-__device__ __forceinline__ void online(T &m, T &s, T z) {
-    if (z > m) {
-        s = Arith<T>::add(Arith<T>::mul(s, Arith<T>::ex(Arith<T>::sub(m, z))), T(1));
-        m = z;
-    } else {
-        s = Arith<T>::add(s, Arith<T>::ex(Arith<T>::sub(z, m)));
-    }
-}
-
+// (m, s) <- the softmax statistics of the items of (m, s) followed by those of
+// (m2, s2): the larger max wins and the other sum is rescaled to it.
 template <typename T>
 __device__ __forceinline__ void combine(T &m, T &s, T m2, T s2) {
     if (m2 == Arith<T>::ninf()) return;
@@ -74,101 +71,400 @@ __device__ __forceinline__ void combine(T &m, T &s, T m2, T s2) {
     }
 }
 
-template <typename T>
-__device__ __forceinline__ int64_t item_id(const SoftArgs<T> &a, int32_t i) {
-    return a.eid ? (int64_t)__ldg(a.eid + i) : (int64_t)i;
+template <typename T, int V>
+__device__ __forceinline__ void put2(T *pa, T *pb, int64_t off, const T (&va)[V], const T (&vb)[V]) {
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+        pa[off + v] = va[v];
+        pb[off + v] = vb[v];
+    }
 }
 
-// One group of UN consecutive items of a lane's column vector.
-template <typename T, int V, int UN>
-struct Group {
-    int64_t e[UN];
-    bool sel[UN];
-    T z[UN][V];
-};
+// Pass 1: per-row (max, 1 / sum) for rows that start and end in the chunk,
+// (max, sum) pieces for the others, and every item's row.
+template <typename T, int V, int CV>
+__global__ void __launch_bounds__(kSoftBlock) k_softmax_stats(const SoftArgs<T> a) {
+    constexpr int W = 32 / CV;  // items per step
+    constexpr int P = BGL_SOFTMAX_DEPTH, R = P + 1;
+    constexpr int SLOT = V * (int)sizeof(T);
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    // ring stage s: this thread's logits at [s][thread], its item's edge id
+    // (for the mask) at [R][...]
+    const uint32_t sbase = smem_addr(smem_raw) + threadIdx.x * SLOT;
+    const T *pbase = reinterpret_cast<const T *>(smem_raw + threadIdx.x * SLOT);
+    int32_t *ebase = reinterpret_cast<int32_t *>(smem_raw + R * kSoftBlock * SLOT) + threadIdx.x;
 
-template <typename T, int V, int UN>
-__device__ __forceinline__ void load_group(const SoftArgs<T> &a, int32_t i0, int32_t ye, int32_t cv,
-                                           Group<T, V, UN> &g) {
+    const int lane = threadIdx.x & 31;
+    const int k = lane / CV, c = lane % CV;
+    const int64_t chunk = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;  // warp-uniform
+    if (chunk >= a.num_chunks) return;
+    const int32_t x0 = (int32_t)a.coords[chunk].x, y0 = (int32_t)a.coords[chunk].y;
+    const int32_t x1 = (int32_t)a.coords[chunk + 1].x, ye = (int32_t)a.coords[chunk + 1].y;
+    const int32_t nrows = a.num_rows;
+    const int64_t d = a.d;
+    // row x0 began in an earlier chunk and ends in this one: its items here
+    // are a head piece; row x1 has items here and goes on: a tail piece
+    const bool x0_before = x0 < nrows && (int32_t)a.indptr[x0] < y0;
+    const bool has_head = x0_before && x0 < x1;
+    const bool has_tail = x1 < nrows && max((int32_t)a.indptr[x1], y0) < ye;
+    const int32_t cvn = a.d / V;
+
+    for (int32_t cb = 0; cb < cvn && y0 < ye; cb += CV) {
+        const int32_t cv = cb + c;
+        const bool live = cv < cvn;
+        const int64_t col = (int64_t)cv * V;
+
+        // the copy side of the ring: step w_copy, this lane's item id fetched
+        // one step ahead of its copy
+        int32_t w_copy = y0, e_next = 0;
+        auto fetch = [&]() {
+            const int32_t i = w_copy + k;
+            if (i < ye) e_next = a.eid ? __ldg(a.eid + i) : i;
+        };
+        auto copy_step = [&](int stage) {
+            const int32_t i = w_copy + k;
+            if (i < ye) {
+                if (live)
+                    cp_async<SLOT>(sbase + stage * kSoftBlock * SLOT,
+                                   a.logits + (int64_t)e_next * d + col);
+                if (a.mask) ebase[stage * kSoftBlock] = e_next;
+            }
+            cp_async_commit();  // an empty group past the chunk end keeps the count
+            w_copy += W;
+            fetch();
+        };
+        fetch();
 #pragma unroll
-    for (int u = 0; u < UN; ++u) {
-        g.sel[u] = false;
-        if (i0 + u < ye) {
-            g.e[u] = item_id(a, i0 + u);
-            g.sel[u] = !a.mask || a.mask[g.e[u]] == 1;
-            if (g.sel[u]) ld_stream(a.logits + g.e[u] * a.d + (int64_t)cv * V, g.z[u]);
+        for (int q = 0; q < P; ++q) copy_step(q);
+
+        int32_t x = x0;             // the row holding the step's first item
+        int32_t carry_row = -1;     // the row left open by the previous step
+        T cm[V], cs[V];             // its (max, sum) so far in this chunk
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+            cm[v] = Arith<T>::ninf();
+            cs[v] = T(0);
+        }
+        int fstage = 0, cstage = P;
+        for (int32_t w0 = y0; w0 < ye; w0 += W) {
+            copy_step(cstage);
+            cp_async_wait<P>();  // the step at w0 has landed
+            const int32_t wend = min(w0 + W, ye);
+            const int32_t i = w0 + k;
+            const bool valid = i < wend;
+
+            // the row of item i: lane j holds the end of row x + j (rows from
+            // x1 on do not end in this chunk)
+            const int32_t endj = (x + lane < x1) ? (int32_t)a.indptr[x + lane + 1] : INT32_MAX;
+            int32_t cnt = 0;
+#pragma unroll
+            for (int step = 16; step > 0; step >>= 1) {
+                const int32_t v = __shfl_sync(kFull, endj, cnt + step - 1);
+                if (v <= i) cnt += step;
+            }
+            int32_t row = x + cnt;
+            int32_t rend = __shfl_sync(kFull, endj, cnt);
+            if (valid && rend <= i) {
+                // past the 32 rows held (a run of empty rows): search the rest
+                int32_t lo = x + 32, hi = x1;
+                while (lo < hi) {
+                    const int32_t mid = lo + ((hi - lo) >> 1);
+                    if ((int32_t)a.indptr[mid + 1] <= i)
+                        lo = mid + 1;
+                    else
+                        hi = mid;
+                }
+                row = lo;
+                rend = lo < x1 ? (int32_t)a.indptr[lo + 1] : INT32_MAX;
+            }
+            if (!valid) row = INT32_MAX;  // joins no item's segment
+
+            T z[V];
+#pragma unroll
+            for (int v = 0; v < V; ++v) z[v] = Arith<T>::ninf();
+            if (valid && live) {
+                bool sel = true;
+                if (a.mask) sel = a.mask[ebase[fstage * kSoftBlock]] == 1;
+                if (sel) {
+                    using VT = typename VecT<T, V>::type;
+                    const VT vv = *reinterpret_cast<const VT *>(pbase + fstage * kSoftBlock * V);
+                    const T *sv = reinterpret_cast<const T *>(&vv);
+#pragma unroll
+                    for (int v = 0; v < V; ++v) z[v] = sv[v];
+                }
+            }
+
+            // segmented max over the step's items of each row
+            T mx[V];
+#pragma unroll
+            for (int v = 0; v < V; ++v) mx[v] = z[v];
+#pragma unroll
+            for (int off = 1; off < W; off <<= 1) {
+                const int32_t orow = __shfl_up_sync(kFull, row, off * CV);
+#pragma unroll
+                for (int v = 0; v < V; ++v) {
+                    const T om = __shfl_up_sync(kFull, mx[v], off * CV);
+                    if (k >= off && orow == row && om > mx[v]) mx[v] = om;
+                }
+            }
+            // the row's max over the step sits at its last item of the step;
+            // the row left open by the previous step takes its running max
+            // into account here, so its sum needs rescaling only when the max
+            // grows
+            const int32_t seg_last = valid ? min(rend, wend) - 1 - w0 : k;
+            const int src = seg_last * CV + c;
+            const bool carried = row == carry_row;
+            T ev[V], M[V];
+#pragma unroll
+            for (int v = 0; v < V; ++v) {
+                M[v] = __shfl_sync(kFull, mx[v], src);
+                if (carried && cm[v] > M[v]) M[v] = cm[v];
+                ev[v] = (valid && M[v] != Arith<T>::ninf())
+                            ? Arith<T>::ex(Arith<T>::sub(z[v], M[v]))
+                            : T(0);
+            }
+            // segmented sum of exp(z - max)
+#pragma unroll
+            for (int off = 1; off < W; off <<= 1) {
+                const int32_t orow = __shfl_up_sync(kFull, row, off * CV);
+#pragma unroll
+                for (int v = 0; v < V; ++v) {
+                    const T oe = __shfl_up_sync(kFull, ev[v], off * CV);
+                    if (k >= off && orow == row) ev[v] = Arith<T>::add(ev[v], oe);
+                }
+            }
+
+            // each row's last item of the step folds in the open row's
+            // statistics and stores the row, its head or tail piece
+            T rm[V], rs[V];
+#pragma unroll
+            for (int v = 0; v < V; ++v) {
+                rm[v] = M[v];
+                rs[v] = ev[v];
+            }
+            if (valid && k == seg_last) {
+                if (carried) {
+#pragma unroll
+                    for (int v = 0; v < V; ++v) {
+                        T prev = cs[v];
+                        if (cm[v] != rm[v])  // the max grew: rescale the earlier sum
+                            prev = cm[v] == Arith<T>::ninf()
+                                       ? T(0)
+                                       : Arith<T>::mul(prev, Arith<T>::ex(Arith<T>::sub(cm[v], rm[v])));
+                        rs[v] = Arith<T>::add(prev, rs[v]);
+                    }
+                }
+                if (live) {
+                    if (rend <= wend) {
+                        if (row == x0 && x0_before) {
+                            put2<T, V>(a.head_m, a.head_s, chunk * d + col, rm, rs);
+                        } else {
+                            T r[V];
+#pragma unroll
+                            for (int v = 0; v < V; ++v) r[v] = Arith<T>::div(T(1), rs[v]);
+                            put2<T, V>(a.row_m, a.row_r, (int64_t)row * d + col, rm, r);
+                        }
+                    } else if (wend == ye) {
+                        put2<T, V>(a.tail_m, a.tail_s, chunk * d + col, rm, rs);
+                    }
+                }
+            }
+            // the row holding the step's last item stays open if it goes on
+            const int ll = (wend - 1 - w0) * CV + c;
+            const int32_t lrow = __shfl_sync(kFull, row, ll);
+            const int32_t lrend = __shfl_sync(kFull, rend, ll);
+#pragma unroll
+            for (int v = 0; v < V; ++v) {
+                const T nm = __shfl_sync(kFull, rm[v], ll);
+                const T ns = __shfl_sync(kFull, rs[v], ll);
+                cm[v] = nm;
+                cs[v] = ns;
+            }
+            carry_row = lrend > wend ? lrow : -1;
+            x = lrow;
+            if (cb == 0 && valid && c == 0) a.item_row[i] = row;
+            fstage = fstage + 1 == R ? 0 : fstage + 1;
+            cstage = cstage + 1 == R ? 0 : cstage + 1;
+        }
+        cp_async_wait<0>();
+    }
+    // row x0 ends here without an item in this chunk: an empty head piece
+    if (has_head && (int32_t)a.indptr[x0 + 1] <= y0) {
+        for (int64_t h = lane; h < d; h += 32) {
+            a.head_m[chunk * d + h] = Arith<T>::ninf();
+            a.head_s[chunk * d + h] = T(0);
         }
     }
-}
-
-template <typename T, int V>
-__device__ __forceinline__ void put_stats(T *pm, T *ps, int64_t slot, int32_t d, int32_t cv,
-                                          const T (&m)[V], const T (&s)[V]) {
-#pragma unroll
-    for (int k = 0; k < V; ++k) {
-        pm[slot * d + (int64_t)cv * V + k] = m[k];
-        ps[slot * d + (int64_t)cv * V + k] = s[k];
+    if (lane == 0) {
+        a.head_row[chunk] = has_head ? x0 : -1;
+        a.tail_row[chunk] = has_tail ? x1 : -1;
     }
 }
 
-// Pass 1: per-row (max, sum) for every row, pieces for split rows.
+// ---------------------------------------------------------------- wide rows
+// With 16 or more lanes per item a step of the warp-wide kernel above covers
+// one or two items and its per-step row search and scans dominate.  Wide rows
+// instead give each chunk to a team of `ts` lanes that walks the chunk's items
+// in CSR order, the gSpMM way: logits come through the same per-lane cp.async
+// ring (groups of UN items, P groups ahead) and every value takes one online
+// (max, sum) update -- a larger value rescales the running sum.
+template <typename T>
+__device__ __forceinline__ void online(T &m, T &s, T z) {
+    if (z > m) {
+        s = Arith<T>::add(Arith<T>::mul(s, Arith<T>::ex(Arith<T>::sub(m, z))), T(1));
+        m = z;
+    } else {
+        s = Arith<T>::add(s, Arith<T>::ex(Arith<T>::sub(z, m)));
+    }
+}
+
+constexpr int kWalkUN = 4;     // items per group
+constexpr int kWalkDepth = 2;  // groups in flight ahead of the fold (60 KB: 3 blocks per SM)
+
 template <typename T, int V>
-__global__ void __launch_bounds__(256, BGL_SOFTMAX_MINB) k_softmax_stats(const SoftArgs<T> a) {
-    constexpr int UN = V == 1 ? 8 : 4;
-    const int ts = a.ts;
+struct WalkRing {
+    static constexpr int R = kWalkDepth + 1;
+    static constexpr int SLOT = V * (int)sizeof(T);
+    // logits slots, then the items' edge ids (int32) for the mask and the stores
+    static constexpr int smem = R * kWalkUN * kSoftBlock * (SLOT + 4);
+};
+
+// The walk shared by both wide-row passes: `on_item(e, i, z)` for every item
+// i (edge id e) of the team's chunk in CSR order, `close_row()` whenever the
+// walk passes a row end (the caller tracks rows).  z is the lane's V logits.
+template <typename T, int V, bool NEED_E, typename OnItem>
+__device__ __forceinline__ void walk_items(const SoftArgs<T> &a, int32_t y0, int32_t ye, int t,
+                                           bool live, int64_t col, OnItem on_item) {
+    using Ring = WalkRing<T, V>;
+    constexpr int UN = kWalkUN, P = kWalkDepth, R = Ring::R, SLOT = Ring::SLOT;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const uint32_t sbase = smem_addr(smem_raw) + threadIdx.x * SLOT;
+    const T *pbase = reinterpret_cast<const T *>(smem_raw + threadIdx.x * SLOT);
+    int32_t *ebase =
+        reinterpret_cast<int32_t *>(smem_raw + R * UN * kSoftBlock * SLOT) + threadIdx.x;
+    auto slot = [](int stage, int u) { return (stage * UN + u) * kSoftBlock; };
+    (void)t;
+
+    int32_t ids[UN];
+    int32_t e_copy = y0;
+    auto fetch_one = [&](int u) { ids[u] = a.eid ? __ldg(a.eid + e_copy + u) : e_copy + u; };
+    auto fetch = [&]() {
+        if (e_copy + UN <= ye) {
+#pragma unroll
+            for (int u = 0; u < UN; ++u) fetch_one(u);
+        } else {
+#pragma unroll
+            for (int u = 0; u < UN; ++u)
+                if (e_copy + u < ye) fetch_one(u);
+        }
+    };
+    auto copy_one = [&](int stage, int u) {
+        if (live) cp_async<SLOT>(sbase + slot(stage, u) * SLOT, a.logits + (int64_t)ids[u] * a.d + col);
+        if (NEED_E || a.mask) ebase[slot(stage, u)] = ids[u];
+    };
+    auto copy_group = [&](int stage) {
+        if (e_copy + UN <= ye) {
+#pragma unroll
+            for (int u = 0; u < UN; ++u) copy_one(stage, u);
+        } else {
+#pragma unroll
+            for (int u = 0; u < UN; ++u)
+                if (e_copy + u < ye) copy_one(stage, u);
+        }
+        cp_async_commit();
+        e_copy += UN;
+        fetch();
+    };
+    auto fold_one = [&](int stage, int u, int32_t i) {
+        const int32_t e = (NEED_E || a.mask) ? ebase[slot(stage, u)] : i;
+        T z[V];
+        using VT = typename VecT<T, V>::type;
+        const VT vv = *reinterpret_cast<const VT *>(pbase + slot(stage, u) * V);
+        const T *sv = reinterpret_cast<const T *>(&vv);
+#pragma unroll
+        for (int v = 0; v < V; ++v) z[v] = sv[v];
+        on_item(e, i, z);
+    };
+    fetch();
+#pragma unroll
+    for (int g = 0; g < P; ++g) copy_group(g);
+    int fstage = 0, cstage = P;
+    for (int32_t i0 = y0; i0 < ye; i0 += UN) {
+        copy_group(cstage);
+        cp_async_wait<P>();
+        if (i0 + UN <= ye) {
+#pragma unroll
+            for (int u = 0; u < UN; ++u) fold_one(fstage, u, i0 + u);
+        } else {
+#pragma unroll
+            for (int u = 0; u < UN; ++u)
+                if (i0 + u < ye) fold_one(fstage, u, i0 + u);
+        }
+        fstage = fstage + 1 == R ? 0 : fstage + 1;
+        cstage = cstage + 1 == R ? 0 : cstage + 1;
+    }
+    cp_async_wait<0>();
+}
+
+// Wide rows, pass 1: (max, 1 / sum) of rows that start and end in the chunk,
+// (max, sum) pieces of the others.
+template <typename T, int V>
+__global__ void __launch_bounds__(kSoftBlock, 3) k_softmax_walk_stats(const SoftArgs<T> a, int ts) {
     const int t = threadIdx.x & (ts - 1);
     const int64_t chunk = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) / ts;
     if (chunk >= a.num_chunks) return;
     const int32_t x0 = (int32_t)a.coords[chunk].x, y0 = (int32_t)a.coords[chunk].y;
     const int32_t x1 = (int32_t)a.coords[chunk + 1].x, ye = (int32_t)a.coords[chunk + 1].y;
+    const int32_t nrows = a.num_rows;
+    const int64_t d = a.d;
     const int32_t cvn = a.d / V;
     int32_t head_row = -1, tail_row = -1;
-    for (int32_t cv = t; cv < cvn; cv += ts) {
+    for (int32_t cb = 0; cb < cvn; cb += ts) {
         int32_t x = x0;
-        if (x >= a.num_rows) break;
+        if (x >= nrows) break;
+        const int32_t cv = cb + t;
+        const bool live = cv < cvn;
+        const int64_t col = (int64_t)cv * V;
         int32_t rs = (int32_t)a.indptr[x];
         int32_t re = (x < x1) ? (int32_t)a.indptr[x + 1] : ye;
         int32_t row_begin = y0;
         T m[V], s[V];
 #pragma unroll
-        for (int k = 0; k < V; ++k) {
-            m[k] = Arith<T>::ninf();
-            s[k] = T(0);
+        for (int v = 0; v < V; ++v) {
+            m[v] = Arith<T>::ninf();
+            s[v] = T(0);
         }
         auto close_row = [&]() {
-            if (row_begin == rs) {
-                put_stats<T, V>(a.row_m, a.row_s, x, a.d, cv, m, s);
-            } else {
-                put_stats<T, V>(a.head_m, a.head_s, chunk, a.d, cv, m, s);
-                head_row = x;
+            if (live) {
+                if (row_begin == rs) {
+                    T r[V];
+#pragma unroll
+                    for (int v = 0; v < V; ++v) r[v] = Arith<T>::div(T(1), s[v]);
+                    put2<T, V>(a.row_m, a.row_r, (int64_t)x * d + col, m, r);
+                } else {
+                    put2<T, V>(a.head_m, a.head_s, chunk * d + col, m, s);
+                }
             }
+            if (row_begin != rs) head_row = x;
             row_begin = re;
             rs = re;
             ++x;
             re = (x < x1) ? (int32_t)a.indptr[x + 1] : ye;
 #pragma unroll
-            for (int k = 0; k < V; ++k) {
-                m[k] = Arith<T>::ninf();
-                s[k] = T(0);
+            for (int v = 0; v < V; ++v) {
+                m[v] = Arith<T>::ninf();
+                s[v] = T(0);
             }
         };
-        for (int32_t i0 = y0; i0 < ye; i0 += UN) {
-            Group<T, V, UN> g;
-            load_group<T, V, UN>(a, i0, ye, cv, g);
+        walk_items<T, V, false>(a, y0, ye, t, live, col, [&](int32_t e, int32_t i, const T(&z)[V]) {
+            while (i >= re) close_row();
+            if (a.mask && a.mask[e] != 1) return;
 #pragma unroll
-            for (int u = 0; u < UN; ++u) {
-                if (i0 + u < ye) {
-                    while (i0 + u >= re) close_row();
-                    if (g.sel[u]) {
-#pragma unroll
-                        for (int k = 0; k < V; ++k) online(m[k], s[k], g.z[u][k]);
-                    }
-                }
-            }
-        }
-        while (x < x1) close_row();
-        if (x < a.num_rows && ye > row_begin) {
-            put_stats<T, V>(a.tail_m, a.tail_s, chunk, a.d, cv, m, s);
+            for (int v = 0; v < V; ++v) online(m[v], s[v], z[v]);
+        });
+        while (x < x1) close_row();  // rows ending at the chunk end, empty rows
+        if (x < nrows && ye > row_begin) {
+            if (live) put2<T, V>(a.tail_m, a.tail_s, chunk * d + col, m, s);
             tail_row = x;
         }
     }
@@ -178,75 +474,132 @@ __global__ void __launch_bounds__(256, BGL_SOFTMAX_MINB) k_softmax_stats(const S
     }
 }
 
-// Pass 2: fold every split row's pieces in CSR order into its row entry.
-template <typename T>
-__global__ void k_softmax_fixup(const SoftArgs<T> a) {
-    const int ts = a.ts;
-    const int t = threadIdx.x & (ts - 1);
-    const int64_t chunk = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) / ts;
-    if (chunk >= a.num_chunks) return;
-    const int32_t row = a.head_row[chunk];
-    if (row < 0) return;
-    int64_t first = chunk;
-    while (first > 0 && a.tail_row[first - 1] == row) --first;
-    for (int32_t h = t; h < a.d; h += ts) {
-        T m = Arith<T>::ninf(), s = T(0);
-        for (int64_t q = first; q < chunk; ++q) combine(m, s, a.tail_m[q * a.d + h], a.tail_s[q * a.d + h]);
-        combine(m, s, a.head_m[chunk * a.d + h], a.head_s[chunk * a.d + h]);
-        a.row_m[(int64_t)row * a.d + h] = m;
-        a.row_s[(int64_t)row * a.d + h] = s;
-    }
-}
-
-// Pass 3: out = exp(z - max) * (1 / sum) over the same chunks; a row's stats
-// are loaded (and its sum inverted) when the walk enters it.
+// Wide rows, pass 2: out = exp(z - max) * (1 / sum) along the same walk; a
+// row's statistics are loaded when the walk enters it, the next row's ahead.
 template <typename T, int V>
-__global__ void __launch_bounds__(256, BGL_SOFTMAX_MINB) k_softmax_write(const SoftArgs<T> a) {
-    constexpr int UN = V == 1 ? 8 : 4;
-    const int ts = a.ts;
+__global__ void __launch_bounds__(kSoftBlock, 3) k_softmax_walk_apply(const SoftArgs<T> a, int ts) {
     const int t = threadIdx.x & (ts - 1);
     const int64_t chunk = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) / ts;
     if (chunk >= a.num_chunks) return;
     const int32_t x0 = (int32_t)a.coords[chunk].x, y0 = (int32_t)a.coords[chunk].y;
     const int32_t ye = (int32_t)a.coords[chunk + 1].y;
+    const int32_t nrows = a.num_rows;
+    const int64_t d = a.d;
     const int32_t cvn = a.d / V;
-    for (int32_t cv = t; cv < cvn; cv += ts) {
+    for (int32_t cb = 0; cb < cvn; cb += ts) {
         int32_t x = x0;
-        if (x >= a.num_rows || y0 >= ye) break;
+        if (x >= nrows || y0 >= ye) break;
+        const int32_t cv = cb + t;
+        const bool live = cv < cvn;
+        const int64_t col = (int64_t)cv * V;
+        // the row holding the chunk's first item (skipping rows that end first)
         int32_t re = (int32_t)a.indptr[x + 1];
-        T m[V], r[V];  // the row's max and the reciprocal of its sum
-        auto load_stats = [&]() {
-            T sum[V];
-            load_vec<T, V>(a.row_m + (int64_t)x * a.d + (int64_t)cv * V, m);
-            load_vec<T, V>(a.row_s + (int64_t)x * a.d + (int64_t)cv * V, sum);
-#pragma unroll
-            for (int k = 0; k < V; ++k) r[k] = Arith<T>::div(T(1), sum[k]);
+        while (y0 >= re) re = (int32_t)a.indptr[++x + 1];
+        T m[V], r[V], nm[V], nr[V];
+        auto load_stats = [&](int32_t row, T(&mm)[V], T(&rr)[V]) {
+            if (live && row < nrows) {
+                load_vec<T, V>(a.row_m + (int64_t)row * d + col, mm);
+                load_vec<T, V>(a.row_r + (int64_t)row * d + col, rr);
+            }
         };
-        while (y0 >= re) {  // rows that end before the first item (empty rows)
-            ++x;
-            re = (int32_t)a.indptr[x + 1];
-        }
-        load_stats();
-        for (int32_t i0 = y0; i0 < ye; i0 += UN) {
-            Group<T, V, UN> g;
-            load_group<T, V, UN>(a, i0, ye, cv, g);
+        load_stats(x, m, r);
+        load_stats(x + 1, nm, nr);
+        walk_items<T, V, true>(a, y0, ye, t, live, col, [&](int32_t e, int32_t i, const T(&z)[V]) {
+            if (i >= re) {
+                const int32_t prev = x;
+                do {
+                    re = (int32_t)a.indptr[++x + 1];
+                } while (i >= re);
+                if (x == prev + 1) {  // the prefetched row
+#pragma unroll
+                    for (int v = 0; v < V; ++v) {
+                        m[v] = nm[v];
+                        r[v] = nr[v];
+                    }
+                } else {
+                    load_stats(x, m, r);
+                }
+                load_stats(x + 1, nm, nr);
+            }
+            if (!live || (a.mask && a.mask[e] != 1)) return;
+            T o[V];
+#pragma unroll
+            for (int v = 0; v < V; ++v)
+                o[v] = Arith<T>::mul(Arith<T>::ex(Arith<T>::sub(z[v], m[v])), r[v]);
+            store_vec<T, V>(a.out + (int64_t)e * d + col, o);
+        });
+    }
+}
+
+// Folds every split row's pieces in CSR order into its (max, 1 / sum).
+template <typename T>
+__global__ void __launch_bounds__(kSoftBlock) k_softmax_fixup(const SoftArgs<T> a) {
+    const int lane = threadIdx.x & 31;
+    const int64_t chunk = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    if (chunk >= a.num_chunks) return;
+    const int32_t row = a.head_row[chunk];
+    if (row < 0) return;
+    int64_t first = chunk;
+    while (first > 0 && a.tail_row[first - 1] == row) --first;
+    const int64_t d = a.d;
+    for (int64_t h = lane; h < d; h += 32) {
+        T m = Arith<T>::ninf(), s = T(0);
+        for (int64_t q = first; q < chunk; ++q) combine(m, s, a.tail_m[q * d + h], a.tail_s[q * d + h]);
+        combine(m, s, a.head_m[chunk * d + h], a.head_s[chunk * d + h]);
+        a.row_m[(int64_t)row * d + h] = m;
+        a.row_r[(int64_t)row * d + h] = Arith<T>::div(T(1), s);
+    }
+}
+
+// Pass 2: out = exp(z - max) * (1 / sum) for every selected item, a team of CV
+// lanes per item, UN items of a team in flight.
+template <typename T, int V, int CV>
+__global__ void __launch_bounds__(kSoftBlock) k_softmax_apply(const SoftArgs<T> a) {
+    constexpr int UN = 4;
+    const int c = (threadIdx.x & 31) % CV;
+    const int64_t team = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) / CV;
+    const int64_t teams = ((int64_t)gridDim.x * blockDim.x) / CV;
+    const int32_t cvn = a.d / V;
+    const int64_t d = a.d;
+    for (int32_t cb = 0; cb < cvn; cb += CV) {
+        const int32_t cv = cb + c;
+        if (cv >= cvn) break;
+        const int64_t col = (int64_t)cv * V;
+        for (int64_t i0 = team; i0 < a.num_items; i0 += teams * UN) {
+            int64_t e[UN];
+            int32_t r[UN];
+            bool ok[UN];
 #pragma unroll
             for (int u = 0; u < UN; ++u) {
-                if (i0 + u < ye) {
-                    if (i0 + u >= re) {
-                        do {
-                            ++x;
-                            re = (int32_t)a.indptr[x + 1];
-                        } while (i0 + u >= re);
-                        load_stats();
-                    }
-                    if (g.sel[u]) {
-                        T o[V];
+                const int64_t i = i0 + u * teams;
+                ok[u] = i < a.num_items;
+                if (ok[u]) {
+                    e[u] = a.eid ? (int64_t)__ldg(a.eid + i) : i;
+                    r[u] = __ldg(a.item_row + i);
+                }
+            }
+            if (a.mask) {
 #pragma unroll
-                        for (int k = 0; k < V; ++k)
-                            o[k] = Arith<T>::mul(Arith<T>::ex(Arith<T>::sub(g.z[u][k], m[k])), r[k]);
-                        store_vec<T, V>(a.out + g.e[u] * a.d + (int64_t)cv * V, o);
-                    }
+                for (int u = 0; u < UN; ++u)
+                    if (ok[u]) ok[u] = a.mask[e[u]] == 1;
+            }
+            T z[UN][V], m[UN][V], rr[UN][V];
+#pragma unroll
+            for (int u = 0; u < UN; ++u) {
+                if (ok[u]) {
+                    ld_stream(a.logits + e[u] * d + col, z[u]);
+                    load_vec<T, V>(a.row_m + (int64_t)r[u] * d + col, m[u]);
+                    load_vec<T, V>(a.row_r + (int64_t)r[u] * d + col, rr[u]);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < UN; ++u) {
+                if (ok[u]) {
+                    T o[V];
+#pragma unroll
+                    for (int v = 0; v < V; ++v)
+                        o[v] = Arith<T>::mul(Arith<T>::ex(Arith<T>::sub(z[u][v], m[u][v])), rr[u][v]);
+                    store_vec<T, V>(a.out + e[u] * d + col, o);
                 }
             }
         }
@@ -254,8 +607,7 @@ __global__ void __launch_bounds__(256, BGL_SOFTMAX_MINB) k_softmax_write(const S
 }
 
 struct SoftPlan {
-    int vmax;
-    int ts;
+    int vmax;  // widest vector the row width allows
     int64_t num_chunks, items, split_min;
 };
 
@@ -263,10 +615,9 @@ SoftPlan softmax_plan(int64_t rows, int64_t items, int64_t d, int dtype) {
     SoftPlan p;
     const int vm = dtype == BGL_F32 ? 4 : 2;
     p.vmax = (d % vm == 0) ? vm : 1;
-    const int64_t cvn = d / p.vmax;
-    p.ts = next_pow2(cvn < 1 ? 1 : cvn);
     const int64_t total = rows + items;
-    int64_t target = int64_t(num_sms()) * 48 * (32 / p.ts) * 3;
+    // one warp per chunk, about four chunks per resident warp
+    int64_t target = int64_t(num_sms()) * 64 * 4;
     const int64_t per_chunk = 4 * (d > 0 ? d : 1) * (dtype == BGL_F32 ? 4 : 8);
     const int64_t cap = (int64_t(256) << 20) / per_chunk;
     if (target > cap) target = cap;
@@ -284,12 +635,13 @@ struct SoftLayout {
     Coord *coords;
     int32_t *head_row, *tail_row;
     T *head_m, *head_s, *tail_m, *tail_s;
-    T *row_m, *row_s;
+    T *row_m, *row_r;
+    int32_t *item_row;
     size_t bytes;
 };
 
 template <typename T>
-SoftLayout<T> softmax_layout(void *ws, const SoftPlan &p, int64_t rows, int64_t d) {
+SoftLayout<T> softmax_layout(void *ws, const SoftPlan &p, int64_t rows, int64_t items, int64_t d) {
     Carver c(ws);
     SoftLayout<T> l;
     l.coords = c.take<Coord>(p.num_chunks + 1);
@@ -300,15 +652,72 @@ SoftLayout<T> softmax_layout(void *ws, const SoftPlan &p, int64_t rows, int64_t 
     l.tail_m = c.take<T>(p.num_chunks * d);
     l.tail_s = c.take<T>(p.num_chunks * d);
     l.row_m = c.take<T>(rows * d);
-    l.row_s = c.take<T>(rows * d);
+    l.row_r = c.take<T>(rows * d);
+    l.item_row = c.take<int32_t>(items);
     l.bytes = c.used + 256;
     return l;
 }
 
 size_t softmax_ws(int64_t rows, int64_t items, int64_t d, int dtype) {
     SoftPlan p = softmax_plan(rows, items, d, dtype);
-    if (dtype == BGL_F32) return softmax_layout<float>(nullptr, p, rows, d).bytes;
-    return softmax_layout<double>(nullptr, p, rows, d).bytes;
+    if (dtype == BGL_F32) return softmax_layout<float>(nullptr, p, rows, items, d).bytes;
+    return softmax_layout<double>(nullptr, p, rows, items, d).bytes;
+}
+
+template <typename T, int V, int CV>
+int launch_softmax(const SoftArgs<T> &a, cudaStream_t s) {
+    constexpr int R = BGL_SOFTMAX_DEPTH + 1;
+    constexpr int smem = R * kSoftBlock * (V * (int)sizeof(T) + 4);
+    auto ks = k_softmax_stats<T, V, CV>;
+    BGL_CUDA(cudaFuncSetAttribute(ks, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    const int64_t threads = a.num_chunks * 32;
+    const int grid = (int)((threads + kSoftBlock - 1) / kSoftBlock);
+    ks<<<grid, kSoftBlock, smem, s>>>(a);
+    BGL_LAUNCH_CHECK();
+    k_softmax_fixup<T><<<grid, kSoftBlock, 0, s>>>(a);
+    BGL_LAUNCH_CHECK();
+    // the item pass: enough teams to fill the GPU a few times over
+    int64_t teams = (int64_t)a.num_items;
+    const int64_t cap = int64_t(num_sms()) * 2048 / CV * 2;
+    if (teams > cap) teams = cap;
+    const int agrid = (int)((teams * CV + kSoftBlock - 1) / kSoftBlock);
+    k_softmax_apply<T, V, CV><<<agrid < 1 ? 1 : agrid, kSoftBlock, 0, s>>>(a);
+    BGL_LAUNCH_CHECK();
+    return BGL_OK;
+}
+
+template <typename T, int V>
+int launch_walk(const SoftArgs<T> &a, int ts, cudaStream_t s) {
+    constexpr int smem = WalkRing<T, V>::smem;
+    auto ks = k_softmax_walk_stats<T, V>;
+    auto ka = k_softmax_walk_apply<T, V>;
+    BGL_CUDA(cudaFuncSetAttribute(ks, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    BGL_CUDA(cudaFuncSetAttribute(ks, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                  cudaSharedmemCarveoutMaxShared));
+    BGL_CUDA(cudaFuncSetAttribute(ka, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    BGL_CUDA(cudaFuncSetAttribute(ka, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                  cudaSharedmemCarveoutMaxShared));
+    const int grid = (int)((a.num_chunks * ts + kSoftBlock - 1) / kSoftBlock);
+    ks<<<grid, kSoftBlock, smem, s>>>(a, ts);
+    BGL_LAUNCH_CHECK();
+    const int fgrid = (int)((a.num_chunks * 32 + kSoftBlock - 1) / kSoftBlock);
+    k_softmax_fixup<T><<<fgrid, kSoftBlock, 0, s>>>(a);
+    BGL_LAUNCH_CHECK();
+    ka<<<grid, kSoftBlock, smem, s>>>(a, ts);
+    BGL_LAUNCH_CHECK();
+    return BGL_OK;
+}
+
+template <typename T, int V>
+int launch_by_cv(const SoftArgs<T> &a, int cv, cudaStream_t s) {
+    // 16 or more lanes per item: the team walk; fewer: the warp-wide steps
+    switch (cv) {
+    case 1: return launch_softmax<T, V, 1>(a, s);
+    case 2: return launch_softmax<T, V, 2>(a, s);
+    case 4: return launch_softmax<T, V, 4>(a, s);
+    case 8: return launch_softmax<T, V, 8>(a, s);
+    default: return launch_walk<T, V>(a, cv, s);
+    }
 }
 
 template <typename T>
@@ -316,32 +725,22 @@ int run_softmax(const int64_t *indptr, const int32_t *eid, const int8_t *mask, i
                 int64_t items, const void *logits, void *out, int64_t d, int dtype, void *ws,
                 cudaStream_t s) {
     SoftPlan p = softmax_plan(rows, items, d, dtype);
-    SoftLayout<T> l = softmax_layout<T>(ws, p, rows, d);
+    SoftLayout<T> l = softmax_layout<T>(ws, p, rows, items, d);
     constexpr int VM = sizeof(T) == 4 ? 4 : 2;
     int V = p.vmax;
     if (V > 1 && (!aligned(logits, V * sizeof(T)) || !aligned(out, V * sizeof(T)))) V = 1;
-    SoftArgs<T> a{indptr,   eid,          mask,       (int32_t)rows, (int32_t)items,
-                  (const T *)logits, (T *)out, (int32_t)d, p.ts,      p.num_chunks,
-                  l.coords, l.head_row,   l.tail_row, l.head_m,      l.head_s,
-                  l.tail_m, l.tail_s,     l.row_m,    l.row_s};
+    const int64_t cvn = d / V;
+    const int cv = next_pow2(cvn > 32 ? 32 : (int)cvn);
+    SoftArgs<T> a{indptr,   eid,        mask,       (int32_t)rows, (int32_t)items,
+                  (const T *)logits, (T *)out, (int32_t)d, p.num_chunks, l.coords,
+                  l.head_row, l.tail_row, l.head_m, l.head_s,      l.tail_m,
+                  l.tail_s, l.row_m,    l.row_r,    l.item_row};
     int cg = (int)((p.num_chunks + 1 + 255) / 256);
     k_spmm_coords<<<cg, 256, 0, s>>>(indptr, rows, items, p.items, p.split_min, p.num_chunks,
                                      l.coords);
     BGL_LAUNCH_CHECK();
-    const int grid = (int)((p.num_chunks * p.ts + 255) / 256);
-    if (V == 1)
-        k_softmax_stats<T, 1><<<grid, 256, 0, s>>>(a);
-    else
-        k_softmax_stats<T, VM><<<grid, 256, 0, s>>>(a);
-    BGL_LAUNCH_CHECK();
-    k_softmax_fixup<T><<<grid, 256, 0, s>>>(a);
-    BGL_LAUNCH_CHECK();
-    if (V == 1)
-        k_softmax_write<T, 1><<<grid, 256, 0, s>>>(a);
-    else
-        k_softmax_write<T, VM><<<grid, 256, 0, s>>>(a);
-    BGL_LAUNCH_CHECK();
-    return BGL_OK;
+    if (V == 1) return launch_by_cv<T, 1>(a, cv, s);
+    return launch_by_cv<T, VM>(a, cv, s);
 }
 
 }  // namespace

@@ -149,6 +149,23 @@ def test_split_rows_float64_and_args(orc, small_chunks):
         np.testing.assert_array_equal(ae, re_)
 
 
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+@pytest.mark.parametrize("heads", [1, 8, 64, 130])
+def test_edge_softmax_split_rows_both_paths(orc, small_chunks, dtype, heads):
+    """Rows split over many merge-path chunks (chunks of ~16 items), for the
+    warp-wide step kernels (narrow rows: 1 and 8 columns) and the team walk
+    (64 and 130 columns, the latter in column blocks), norm_by dst and src."""
+    u, v = power_law(3000, 37)
+    rng = np.random.default_rng(38)
+    z = (rng.normal(size=(u.size, heads, 1)) * 3).astype(dtype)
+    g, og = dgl.graph((u, v)), orc.Graph(u, v)
+    rtol = 2e-5 if dtype == np.float32 else 1e-12
+    for norm_by in ("dst", "src"):
+        got = ops.edge_softmax(g, z, norm_by=norm_by)
+        want = orc.edge_softmax(og, z.astype(np.float64), norm_by=norm_by)
+        np.testing.assert_allclose(got, want, rtol=rtol, atol=1e-7 if dtype == np.float32 else 0)
+
+
 def test_split_rows_are_deterministic(small_chunks):
     u, v = power_law(5000, 41)
     x = np.random.default_rng(42).normal(size=(5000, 64)).astype(np.float32)
