@@ -152,64 +152,6 @@ struct Operand {
     bool uniform;  // div % V == 0: one element serves a whole output vector
 };
 
-// Where a broadcast operand's values for a lane's V output columns
-// [k0, k0 + V) live in its row: resolved once per lane (its columns do not
-// change while it walks edges), so the broadcast's divide and modulo stay out
-// of the gather loop.  A full operand needs no map: its offset is k0 itself,
-// recomputed in the loop, which keeps one less register live.
-template <int V>
-struct ColMap {
-    // uniform broadcast: the one operand column all V outputs read;
-    // otherwise the lane's first output column
-    int32_t off;
-};
-
-template <typename T, int V>
-__device__ __forceinline__ ColMap<V> col_map(const Operand<T> &o, int64_t k0) {
-    ColMap<V> m;
-    m.off = (o.full || !o.uniform) ? (int32_t)k0
-                                   : (int32_t)(((uint32_t)k0 / (uint32_t)o.div) % (uint32_t)o.width);
-    return m;
-}
-
-// Loads the lane's V output columns [k0, k0 + V) of operand row `row`.
-template <typename T, int V>
-__device__ __forceinline__ void load_mapped(const Operand<T> &o, int64_t row, int64_t k0,
-                                            const ColMap<V> &m, T (&r)[V]) {
-    const T *base = o.ptr + row * o.width;
-    if (o.full) {
-        ld_stream(base + k0, r);
-    } else if (o.uniform) {
-        T x = __ldg(base + m.off);
-#pragma unroll
-        for (int i = 0; i < V; ++i) r[i] = x;
-    } else {
-#pragma unroll
-        for (int i = 0; i < V; ++i)
-            r[i] = __ldg(base + ((uint32_t)(m.off + i) / (uint32_t)o.div) % (uint32_t)o.width);
-    }
-}
-
-// Loads output columns [k0, k0 + V) of operand row `row`.  Row widths and
-// broadcast divisors are below 2^31, so the broadcast's column arithmetic is
-// done in 32-bit unsigned integers (a fraction of the 64-bit divide's cost).
-template <typename T, int V>
-__device__ __forceinline__ void load_cols(const Operand<T> &o, int64_t row, int64_t k0,
-                                          T (&r)[V]) {
-    const T *base = o.ptr + row * o.width;
-    if (o.full) {
-        ld_stream(base + k0, r);
-    } else if (o.uniform) {
-        T x = __ldg(base + ((uint32_t)k0 / (uint32_t)o.div) % (uint32_t)o.width);
-#pragma unroll
-        for (int i = 0; i < V; ++i) r[i] = x;
-    } else {
-#pragma unroll
-        for (int i = 0; i < V; ++i)
-            r[i] = __ldg(base + ((uint32_t)(k0 + i) / (uint32_t)o.div) % (uint32_t)o.width);
-    }
-}
-
 inline bool aligned(const void *p, size_t a) {
     return (reinterpret_cast<uintptr_t>(p) % a) == 0;
 }
@@ -299,6 +241,26 @@ __device__ __forceinline__ void stage_row(const LaneCols<T, V> &c, const Operand
         for (int i = 0; i < V; ++i)
             cp_async<sizeof(T)>(dst + i * sizeof(T),
                                 r + ((uint32_t)(c.k0 + i) / (uint32_t)o.div) % (uint32_t)o.width);
+    }
+}
+
+// Loads the lane's values of operand row `row` into registers (the same
+// addressing as stage_row, for kernels without a gather ring).
+template <typename T, int V>
+__device__ __forceinline__ void load_row(const LaneCols<T, V> &c, const Operand<T> &o, int64_t row,
+                                         T (&r)[V]) {
+    const char *src = c.base + (uint64_t)row * c.row_bytes;
+    if (c.mode == 0) {
+        ld_stream(reinterpret_cast<const T *>(src), r);
+    } else if (c.mode == 1) {
+        const T x = __ldg(reinterpret_cast<const T *>(src));
+#pragma unroll
+        for (int i = 0; i < V; ++i) r[i] = x;
+    } else {
+        const T *p = reinterpret_cast<const T *>(src);
+#pragma unroll
+        for (int i = 0; i < V; ++i)
+            r[i] = __ldg(p + ((uint32_t)(c.k0 + i) / (uint32_t)o.div) % (uint32_t)o.width);
     }
 }
 

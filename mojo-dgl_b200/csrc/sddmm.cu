@@ -2,10 +2,13 @@
 //
 // Edge-parallel: a team of lanes per edge, each lane owning V consecutive
 // output columns; the two operand rows are gathered through the target code
-// (u[e], v[e] or e itself, src/ported.mojo:256-271).  `dot` accumulates the
-// lane's products and folds the team's partials with xor shuffles, so unlike
-// the element-wise ops its rounding differs from the reference's lane-partial
-// order (src/ported.mojo:273-293) -- it is compared with a tolerance.
+// (u[e], v[e] or e itself, src/ported.mojo:256-271).  A team takes UN edges
+// per iteration -- their ids first, then all their row loads, then the
+// arithmetic and the stores -- so each lane keeps UN row pairs in flight.
+// `dot` accumulates the lane's products and folds the team's partials with
+// xor shuffles, so unlike the element-wise ops its rounding differs from the
+// reference's lane-partial order (src/ported.mojo:273-293) -- it is compared
+// with a tolerance.
 #include "common.cuh"
 
 namespace bgl {
@@ -31,8 +34,22 @@ __device__ __forceinline__ int64_t target_row(int tgt, const int32_t *u, const i
     return e;
 }
 
+// Random whole-row gathers want resident warps more than per-warp depth.
+// Measured on config 5 (u_dot_v, 50M edges, two 5 GB (N, 256) float32
+// matrices): one edge per team at 8 blocks of 256 per SM (32 registers)
+// 15.7 ms; 2 edges at 4 blocks 20.9 ms; 4 at 3 blocks 23.9 ms; 4 at 2 blocks
+// 37.1 ms.  Config 2's u_add_v (8 columns): 0.567 / 0.576 / 0.604 / 0.726 ms.
+#ifndef BGL_SDDMM_UN
+#define BGL_SDDMM_UN 1  // edges a team has in flight
+#endif
+#ifndef BGL_SDDMM_MINB
+#define BGL_SDDMM_MINB 8  // resident 256-thread blocks per SM the registers must allow
+#endif
+constexpr int kSddmmUN = BGL_SDDMM_UN;
+
 template <typename T, int OP, int V>
-__global__ void __launch_bounds__(256) k_sddmm(const SddmmArgs<T> a) {
+__global__ void __launch_bounds__(256, BGL_SDDMM_MINB) k_sddmm(const SddmmArgs<T> a) {
+    constexpr int UN = kSddmmUN;
     const int ts = a.ts;
     const int lane = threadIdx.x & 31;
     const int t = lane & (ts - 1);
@@ -41,42 +58,85 @@ __global__ void __launch_bounds__(256) k_sddmm(const SddmmArgs<T> a) {
     const int64_t teams = ((int64_t)gridDim.x * blockDim.x) / ts;
     constexpr bool NEED_L = OP != BGL_OP_COPY_RHS;
     constexpr bool NEED_R = OP != BGL_OP_COPY_LHS;
-    ColMap<V> lmap, rmap;
-    if (OP != BGL_OP_DOT) {
-        if (NEED_L) lmap = col_map<T, V>(a.lhs, (int64_t)t * V);
-        if (NEED_R) rmap = col_map<T, V>(a.rhs, (int64_t)t * V);
-    }
-    for (int64_t e = team; e < a.num_edges; e += teams) {
-        const int64_t li = NEED_L ? target_row(a.lt, a.u, a.v, e) : 0;
-        const int64_t ri = NEED_R ? target_row(a.rt, a.u, a.v, e) : 0;
-        if (OP == BGL_OP_DOT) {
-            T acc = T(0);
-            const int64_t cvn = a.red_len / V;
-            for (int64_t cv = t; cv < cvn; cv += ts) {
-                T l[V], r[V];
-                load_vec<T, V>(a.lhs.ptr + li * a.red_len + cv * V, l);
-                load_vec<T, V>(a.rhs.ptr + ri * a.red_len + cv * V, r);
+    if (OP == BGL_OP_DOT) {
+        const int32_t cvn = (int32_t)(a.red_len / V);
+        for (int64_t e0 = team; e0 < a.num_edges; e0 += teams * UN) {
+            int64_t li[UN], ri[UN];
+            bool ok[UN];
 #pragma unroll
-                for (int i = 0; i < V; ++i) acc = Arith<T>::add(acc, Arith<T>::mul(l[i], r[i]));
+            for (int u = 0; u < UN; ++u) {
+                const int64_t e = e0 + u * teams;
+                ok[u] = e < a.num_edges;
+                li[u] = ok[u] ? target_row(a.lt, a.u, a.v, e) : 0;
+                ri[u] = ok[u] ? target_row(a.rt, a.u, a.v, e) : 0;
             }
-            for (int off = ts >> 1; off > 0; off >>= 1)
-                acc = Arith<T>::add(acc, __shfl_xor_sync(mask, acc, off, ts));
-            if (t == 0) a.out[e] = acc;
-        } else {
-            const int64_t cvn = a.dout / V;
-            for (int64_t cv = t; cv < cvn; cv += ts) {
-                T l[V], r[V], o[V];
-                if (cv == t) {  // the lane's first columns: the common, one-vector case
-                    if (NEED_L) load_mapped<T, V>(a.lhs, li, (int64_t)t * V, lmap, l);
-                    if (NEED_R) load_mapped<T, V>(a.rhs, ri, (int64_t)t * V, rmap, r);
-                } else {
-                    if (NEED_L) load_cols<T, V>(a.lhs, li, cv * V, l);
-                    if (NEED_R) load_cols<T, V>(a.rhs, ri, cv * V, r);
+            T acc[UN];
+#pragma unroll
+            for (int u = 0; u < UN; ++u) acc[u] = T(0);
+            for (int32_t cv = t; cv < cvn; cv += ts) {
+                T l[UN][V], r[UN][V];
+#pragma unroll
+                for (int u = 0; u < UN; ++u) {
+                    if (ok[u]) {
+                        ld_stream(a.lhs.ptr + li[u] * a.red_len + (int64_t)cv * V, l[u]);
+                        ld_stream(a.rhs.ptr + ri[u] * a.red_len + (int64_t)cv * V, r[u]);
+                    }
                 }
 #pragma unroll
-                for (int i = 0; i < V; ++i)
-                    o[i] = message<OP, T>(NEED_L ? l[i] : T(0), NEED_R ? r[i] : T(0));
-                store_vec<T, V>(a.out + e * a.dout + cv * V, o);
+                for (int u = 0; u < UN; ++u) {
+                    if (ok[u]) {
+#pragma unroll
+                        for (int i = 0; i < V; ++i)
+                            acc[u] = Arith<T>::add(acc[u], Arith<T>::mul(l[u][i], r[u][i]));
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < UN; ++u) {
+                for (int off = ts >> 1; off > 0; off >>= 1)
+                    acc[u] = Arith<T>::add(acc[u], __shfl_xor_sync(mask, acc[u], off, ts));
+                if (ok[u] && t == 0) a.out[e0 + u * teams] = acc[u];
+            }
+        }
+        return;
+    }
+    const int32_t cvn = (int32_t)(a.dout / V);
+    for (int32_t cb = 0; cb < cvn; cb += ts) {
+        const int32_t cv = cb + t;
+        if (cv >= cvn) break;  // no shuffles below: lanes may leave
+        const int64_t k0 = (int64_t)cv * V;
+        LaneCols<T, V> lc, rc;
+        if (NEED_L) lc = lane_cols<T, V>(a.lhs, k0);
+        if (NEED_R) rc = lane_cols<T, V>(a.rhs, k0);
+        for (int64_t e0 = team; e0 < a.num_edges; e0 += teams * UN) {
+            int64_t li[UN], ri[UN];
+            bool ok[UN];
+#pragma unroll
+            for (int u = 0; u < UN; ++u) {
+                const int64_t e = e0 + u * teams;
+                ok[u] = e < a.num_edges;
+                if (ok[u]) {
+                    if (NEED_L) li[u] = target_row(a.lt, a.u, a.v, e);
+                    if (NEED_R) ri[u] = target_row(a.rt, a.u, a.v, e);
+                }
+            }
+            T l[UN][V], r[UN][V];
+#pragma unroll
+            for (int u = 0; u < UN; ++u) {
+                if (ok[u]) {
+                    if (NEED_L) load_row<T, V>(lc, a.lhs, li[u], l[u]);
+                    if (NEED_R) load_row<T, V>(rc, a.rhs, ri[u], r[u]);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < UN; ++u) {
+                if (ok[u]) {
+                    T o[V];
+#pragma unroll
+                    for (int i = 0; i < V; ++i)
+                        o[i] = message<OP, T>(NEED_L ? l[u][i] : T(0), NEED_R ? r[u][i] : T(0));
+                    store_vec<T, V>(a.out + (e0 + u * teams) * a.dout + k0, o);
+                }
             }
         }
     }
@@ -84,8 +144,10 @@ __global__ void __launch_bounds__(256) k_sddmm(const SddmmArgs<T> a) {
 
 template <typename T, int V>
 int launch_sddmm(const SddmmArgs<T> &a, int op, cudaStream_t s) {
-    int64_t teams = a.num_edges;
-    int64_t cap = int64_t(num_sms()) * 2048 / a.ts;  // one full wave of resident teams
+    // two waves of resident teams (3 blocks of 256 per SM); each keeps UN
+    // edges in flight
+    int64_t teams = (a.num_edges + kSddmmUN - 1) / kSddmmUN;
+    const int64_t cap = int64_t(num_sms()) * 256 * BGL_SDDMM_MINB * 2 / a.ts;
     if (teams > cap) teams = cap;
     int grid = (int)((teams * a.ts + 255) / 256);
     if (grid < 1) grid = 1;
@@ -157,6 +219,11 @@ extern "C" int bgl_gsddmm(const int32_t *u, const int32_t *v, int64_t num_edges,
     if (op != BGL_OP_DOT && ((need_l && (lhs_width < 1 || lhs_div < 1)) ||
                              (need_r && (rhs_width < 1 || rhs_div < 1))))
         return fail(BGL_E_INVALID, "bgl_gsddmm: operand width/div must be >= 1");
+    // 32-bit row strides: feature rows below 4 GiB, broadcast arithmetic below 2^31
+    const int64_t elem = dtype == BGL_F32 ? 4 : 8, lim = int64_t(1) << 31;
+    if (dout >= lim || red_len >= lim || (need_l && (lhs_width * elem >= 2 * lim || lhs_div >= lim)) ||
+        (need_r && (rhs_width * elem >= 2 * lim || rhs_div >= lim)))
+        return fail(BGL_E_UNSUPPORTED, "bgl_gsddmm: a feature row of 4 GiB or more");
     if (num_edges == 0 || dout == 0) return BGL_OK;
     if (!out || (need_l && !lhs) || (need_r && !rhs))
         return fail(BGL_E_INVALID, "bgl_gsddmm: null buffer");
