@@ -272,12 +272,14 @@ __global__ void __launch_bounds__(kSpmmBlock, (Stages<T, OP, V>::minb)) k_spmm(c
     constexpr bool NEED_L = OP != BGL_OP_COPY_RHS;
     constexpr bool NEED_R = OP != BGL_OP_COPY_LHS;
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    // slot (stage, u, operand) of this thread: lanes of a warp are adjacent,
-    // so the copies and the read-backs are conflict-free
-    const uint32_t sbase = smem_addr(smem_raw) + threadIdx.x * S::slot;
-    const T *pbase = reinterpret_cast<const T *>(smem_raw + threadIdx.x * S::slot);
-    auto slot_off = [](int stage, int u, int op) {
-        return ((stage * UN + u) * S::nops + op) * kSpmmBlock * S::slot;
+    // each operand has its own region of slots (stage, u, thread), packed at
+    // the size the operand copies per lane -- V values, or one for a uniform
+    // broadcast -- so the lanes of a warp touch adjacent words: the copies and
+    // the read-backs are free of bank conflicts
+    const uint32_t s0 = smem_addr(smem_raw);
+    constexpr uint32_t region = (uint32_t)R * UN * kSpmmBlock * S::slot;
+    auto slot_at = [](int stage, int u, int op, uint32_t stride) -> uint32_t {
+        return op * region + ((uint32_t)(stage * UN + u) * kSpmmBlock + threadIdx.x) * stride;
     };
 
     const int ts = a.ts;
@@ -335,8 +337,15 @@ __global__ void __launch_bounds__(kSpmmBlock, (Stages<T, OP, V>::minb)) k_spmm(c
 
         // the lane's columns of each operand, fixed for the walk
         LaneCols<T, V> lc, rc;
-        if (NEED_L) lc = lane_cols<T, V>(a.lhs, k0);
-        if (NEED_R) rc = lane_cols<T, V>(a.rhs, k0);
+        uint32_t lstride = S::slot, rstride = S::slot;  // bytes per slot
+        if (NEED_L) {
+            lc = lane_cols<T, V>(a.lhs, k0);
+            if (lc.mode == 1) lstride = sizeof(T);
+        }
+        if (NEED_R) {
+            rc = lane_cols<T, V>(a.rhs, k0);
+            if (rc.mode == 1) rstride = sizeof(T);
+        }
 
         // ids of the next group to copy, fetched one group ahead of its copy;
         // only a chunk's last group needs a bound on every edge
@@ -357,8 +366,9 @@ __global__ void __launch_bounds__(kSpmmBlock, (Stages<T, OP, V>::minb)) k_spmm(c
             }
         };
         auto copy_one = [&](int stage, int u) {
-            if (NEED_L) stage_row<T, V>(lc, a.lhs, src[u], sbase + slot_off(stage, u, 0));
-            if (NEED_R) stage_row<T, V>(rc, a.rhs, edg[u], sbase + slot_off(stage, u, S::nops - 1));
+            if (NEED_L) stage_row<T, V>(lc, a.lhs, src[u], s0 + slot_at(stage, u, 0, lstride));
+            if (NEED_R)
+                stage_row<T, V>(rc, a.rhs, edg[u], s0 + slot_at(stage, u, S::nops - 1, rstride));
         };
         auto copy_group = [&](int stage) {
             if (live) {  // a lane past the row's last column copies nothing
@@ -380,8 +390,11 @@ __global__ void __launch_bounds__(kSpmmBlock, (Stages<T, OP, V>::minb)) k_spmm(c
         auto fold_one = [&](int stage, int u, int32_t e) {
             while (e >= re) close_row();
             T lv[V], rv[V];
-            if (NEED_L) read_row<T, V>(lc, pbase + slot_off(stage, u, 0) / sizeof(T), lv);
-            if (NEED_R) read_row<T, V>(rc, pbase + slot_off(stage, u, S::nops - 1) / sizeof(T), rv);
+            if (NEED_L)
+                read_row<T, V>(lc, reinterpret_cast<const T *>(smem_raw + slot_at(stage, u, 0, lstride)), lv);
+            if (NEED_R)
+                read_row<T, V>(rc, reinterpret_cast<const T *>(
+                                       smem_raw + slot_at(stage, u, S::nops - 1, rstride)), rv);
 #pragma unroll
             for (int i = 0; i < V; ++i) {
                 T m = message<OP, T>(NEED_L ? lv[i] : T(0), NEED_R ? rv[i] : T(0));
