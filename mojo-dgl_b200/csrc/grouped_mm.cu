@@ -47,14 +47,34 @@ __global__ void k_zero_tail(T *__restrict__ out, const int64_t *__restrict__ seg
         out[i] = T(0);
 }
 
+// Sort keys, the identity permutation and the rows per relation.  With few
+// relations (r <= kKeysSmem) each block counts in shared memory and adds its
+// counts once, instead of every row hitting one of r global counters.
+constexpr int kKeysSmem = 8192;
+
 __global__ void k_gmm_keys(const int64_t *__restrict__ idx, int32_t *__restrict__ key,
-                           int32_t *__restrict__ iota, int64_t *__restrict__ counts, int64_t n) {
+                           int32_t *__restrict__ iota, int64_t *__restrict__ counts, int64_t n,
+                           int64_t r) {
+    extern __shared__ unsigned int hist[];
+    const bool local = r <= kKeysSmem;
+    if (local) {
+        for (int64_t j = threadIdx.x; j < r; j += blockDim.x) hist[j] = 0;
+        __syncthreads();
+    }
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
         int32_t k = (int32_t)idx[i];
         key[i] = k;
         iota[i] = (int32_t)i;
-        atomicAdd(reinterpret_cast<unsigned long long *>(counts + k), 1ull);
+        if (local)
+            atomicAdd(&hist[k], 1u);
+        else
+            atomicAdd(reinterpret_cast<unsigned long long *>(counts + k), 1ull);
+    }
+    if (local) {
+        __syncthreads();
+        for (int64_t j = threadIdx.x; j < r; j += blockDim.x)
+            if (hist[j]) atomicAdd(reinterpret_cast<unsigned long long *>(counts + j), (unsigned long long)hist[j]);
     }
 }
 
@@ -269,7 +289,8 @@ int bgl_gather_mm(const void *a, const void *b, const int64_t *idx_b, void *out,
     BGL_CUDA(cudaMemsetAsync(l.counts, 0, size_t(r) * sizeof(int64_t), s));
     int g = (int)((n + 255) / 256);
     if (g > num_sms() * 16) g = num_sms() * 16;
-    k_gmm_keys<<<g, 256, 0, s>>>(idx_b, l.keys, l.iota, l.counts, n);
+    const size_t hist_bytes = r <= kKeysSmem ? size_t(r) * sizeof(unsigned int) : 0;
+    k_gmm_keys<<<g, 256, hist_bytes, s>>>(idx_b, l.keys, l.iota, l.counts, n, r);
     BGL_LAUNCH_CHECK();
     int bits = 1;
     while (bits < 31 && (int64_t(1) << bits) < r) ++bits;

@@ -1,19 +1,22 @@
 // tcgen05 grouped GEMM for segment_mm / gather_mm (replaces the serial
 // src/ported.mojo:773-804 and the per-row src/ported.mojo:1089-1130).
 //
-// One CTA computes a 128-row x BN-column tile of one segment: A rows are
-// streamed by TMA in 128-byte K slices (32 fp32 or 64 bf16 values, SWIZZLE_128B),
-// B is the segment's (K x N) block pre-transposed to K-major (N rows of K) so
-// both operands use the canonical K-major swizzled layout; one elected thread
-// issues tcgen05.mma (kind::tf32 for fp32 inputs, kind::f16 with bf16 for
-// bf16 inputs) into a 128 x BN fp32 accumulator in tensor memory; the four
-// warps then read it back with tcgen05.ld (32 lanes each) and store their rows
-// (scattered through `perm` for gather_mm).  Two pipeline stages per CTA and
-// two CTAs per SM let one CTA's epilogue overlap the other's loads.
+// A persistent, warp-specialised kernel, one CTA per SM walking 128-row x
+// BN-column tiles (a tile never crosses a segment).  Warp 0 streams A rows and
+// the segment's K-major B block by TMA in 128-byte K slices (32 fp32 or 64
+// bf16 values, SWIZZLE_128B) through a ring of kStages stages; warp 1 (one
+// elected thread) issues tcgen05.mma (kind::tf32 for fp32 inputs, kind::f16
+// with bf16 for bf16 inputs) into one of two 128 x BN fp32 accumulators in
+// tensor memory; warps 2-5 read the other accumulator back with tcgen05.ld
+// (each warp its 32-lane quarter), transpose them through shared memory and
+// store whole row segments (rows scattered through `perm` for gather_mm)
+// while the next tile's loads and MMAs run.
 //
-// Every mbarrier wait is bounded (kTimeoutNs of %globaltimer); on
-// expiry the CTA records an error code in g_bgl_tc_error, stops issuing,
-// drains what it issued (again bounded), frees its tensor memory and exits.
+// Every mbarrier wait is bounded (kTimeoutNs of %globaltimer); the first to
+// expire records an error code in g_bgl_tc_error and raises a CTA-wide abort
+// flag that ends every role's loop; the producer then waits (bounded) for the
+// loads it issued and the MMA thread for the MMAs it issued, so no copy or MMA
+// is in flight when the tensor memory is freed and the CTA exits.
 #include <cuda.h>
 #include <cuda_bf16.h>
 
@@ -28,8 +31,9 @@ __device__ int g_bgl_tc_error = 0;
 namespace {
 
 constexpr int kBM = 128;
-constexpr int kStages = 2;
-constexpr int kThreads = 128;
+constexpr int kStages = 4;
+constexpr int kThreads = 192;  // producer warp, MMA warp, 4 epilogue warps
+constexpr int kStageRowBytes = 128;  // epilogue staging: 32 fp32 (or bf16 pairs) per row
 constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -58,17 +62,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait: false (and the error word set) if the phase never completes.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int code) {
+// Bounded wait: false if the phase has not completed within kTimeoutNs (the
+// error word and the CTA's abort flag are then set) or if another role of the
+// CTA has aborted (abort == nullptr: wait regardless of the flag).
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int code,
+                                          volatile int *abort) {
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = now_ns();
     while (!mbar_try_wait(bar, parity)) {
+        if (abort && *abort) return false;
         if (now_ns() - t0 > kTimeoutNs) {
             atomicCAS(&g_bgl_tc_error, 0, code);
+            if (abort) *abort = 1;
             return false;
         }
     }
     return true;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
@@ -119,12 +132,17 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
                  : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld8(uint32_t addr, uint32_t (&r)[8]) {
+// 16 consecutive fp32 columns of the warp's 32 TMEM lanes (one row a thread).
+__device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t (&r)[16]) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15}, [%16];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-          "=r"(r[7])
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15])
         : "r"(addr));
+}
+__device__ __forceinline__ void tmem_wait_ld() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
@@ -139,6 +157,7 @@ struct TcArgs {
     int32_t d2;
     int32_t bn;      // N columns of one CTA tile (multiple of 16, <= 256)
     int32_t kb;      // number of 128-byte K slices
+    int32_t nbn;     // column tiles per row tile
 };
 
 // Instruction descriptor: fp32 accumulator, A/B format (TF32 = 2, BF16 = 1),
@@ -148,47 +167,60 @@ __host__ __device__ constexpr uint32_t instr_desc(bool bf16, int n) {
            ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
 }
 
-template <bool BF16>
-__global__ void __launch_bounds__(kThreads, 2)
-    k_gmm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-             const TcArgs args) {
-    extern __shared__ __align__(1024) unsigned char smem_raw[];
-    const int64_t tile = blockIdx.x;
-    if (tile >= args.tile_off[args.r]) return;
+// Row tile `tile` -> (segment, first row, end of the segment's rows).
+__device__ __forceinline__ void tile_rows(const TcArgs &args, int64_t tile, int64_t &rel,
+                                          int64_t &row0, int64_t &row_end) {
     int64_t lo = 0, hi = args.r;
     while (lo < hi) {
         int64_t mid = (lo + hi + 1) >> 1;
         if (args.tile_off[mid] <= tile) lo = mid; else hi = mid - 1;
     }
-    const int64_t rel = lo;
-    const int64_t row0 = args.seg_off[rel] + (tile - args.tile_off[rel]) * kBM;
-    const int64_t row_end = args.seg_off[rel + 1];
-    const int32_t nb = blockIdx.y;
+    rel = lo;
+    row0 = args.seg_off[rel] + (tile - args.tile_off[rel]) * kBM;
+    row_end = args.seg_off[rel + 1];
+}
 
+template <bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_gmm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+             const TcArgs args) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t row_tiles = args.tile_off[args.r];
+    const int64_t work = row_tiles * args.nbn;  // (row tile, column tile) pairs
     const uint32_t a_bytes = kBM * 128, b_bytes = (uint32_t)args.bn * 128;
     // stage buffers, each 1024-byte aligned (the SWIZZLE_128B atom)
     uintptr_t base = (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023);
     unsigned char *sa = reinterpret_cast<unsigned char *>(base);
     unsigned char *sb = sa + kStages * a_bytes;
-    uint64_t *full = reinterpret_cast<uint64_t *>(sb + kStages * b_bytes);
+    // epilogue staging: per epilogue warp 32 rows x 128 bytes
+    uint4 *staging = reinterpret_cast<uint4 *>(sb + kStages * b_bytes);
+    uint64_t *full = reinterpret_cast<uint64_t *>(sb + kStages * b_bytes + 4 * kStageRowBytes * 32);
     uint64_t *empty = full + kStages;
-    uint64_t *accum = empty + kStages;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum + 1);
+    uint64_t *acc_full = empty + kStages;  // [2]: accumulator b holds a finished tile
+    uint64_t *acc_empty = acc_full + 2;    // [2]: the epilogue has read accumulator b
+    uint64_t *mma_done = acc_empty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
+    volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(accum, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 4);  // one arrive per epilogue warp
+        }
+        mbar_init(mma_done, 1);
+        *abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    const uint32_t tmem_cols = args.bn <= 32 ? 32 : args.bn <= 64 ? 64 : args.bn <= 128 ? 128 : 256;
+    const uint32_t acc_cols = args.bn <= 32 ? 32 : args.bn <= 64 ? 64 : args.bn <= 128 ? 128 : 256;
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(tmem_slot)),
-                     "r"(tmem_cols));
+                     "r"(2 * acc_cols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -197,68 +229,128 @@ __global__ void __launch_bounds__(kThreads, 2)
     const uint32_t tmem = *tmem_slot;
     const int kb_n = args.kb;
 
-    if (warp == 0 && lane == 0) {
-        // TMA producer
-        int issued = 0;
-        for (int kb = 0; kb < kb_n; ++kb) {
-            const int s = kb % kStages;
-            if (kb >= kStages && !mbar_wait(&empty[s], ((kb / kStages) - 1) & 1, 1)) break;
-            mbar_arrive_expect_tx(&full[s], a_bytes + b_bytes);
-            const int32_t kx = kb * (BF16 ? 64 : 32);
-            tma_load_2d(sa + s * a_bytes, &map_a, &full[s], kx, (int32_t)row0);
-            tma_load_2d(sb + s * b_bytes, &map_b, &full[s], kx,
-                        (int32_t)(rel * args.d2 + (int64_t)nb * args.bn));
-            issued = kb + 1;
+    if (warp == 0) {
+        if (lane == 0) {
+            // TMA producer: k-iteration `it` counts across this CTA's tiles
+            int64_t it = 0;
+            bool ok = true;
+            for (int64_t w = blockIdx.x; w < work && ok; w += gridDim.x) {
+                int64_t rel, row0, row_end;
+                tile_rows(args, w / args.nbn, rel, row0, row_end);
+                const int32_t nb = (int32_t)(w % args.nbn);
+                for (int kb = 0; kb < kb_n; ++kb, ++it) {
+                    const int s = (int)(it % kStages);
+                    if (it >= kStages &&
+                        !(ok = mbar_wait(&empty[s], (uint32_t)((it / kStages) - 1) & 1, 1, abort)))
+                        break;
+                    mbar_arrive_expect_tx(&full[s], a_bytes + b_bytes);
+                    const int32_t kx = kb * (BF16 ? 64 : 32);
+                    tma_load_2d(sa + s * a_bytes, &map_a, &full[s], kx, (int32_t)row0);
+                    tma_load_2d(sb + s * b_bytes, &map_b, &full[s], kx,
+                                (int32_t)(rel * args.d2 + (int64_t)nb * args.bn));
+                }
+            }
+            // the last issued loads (at most one per stage) have landed before exit
+            for (int64_t j = (it > kStages ? it - kStages : 0); j < it; ++j)
+                mbar_wait(&full[j % kStages], (uint32_t)(j / kStages) & 1, 2, nullptr);
         }
-        // drain: every issued stage's loads must have landed before exit
-        for (int kb = (issued > kStages ? issued - kStages : 0); kb < issued; ++kb)
-            mbar_wait(&full[kb % kStages], (kb / kStages) & 1, 2);
-    } else if (warp == 1 && lane == 0) {
-        // MMA issuer
-        const uint32_t idesc = instr_desc(BF16, args.bn);
-        bool ok = true;
-        for (int kb = 0; kb < kb_n && ok; ++kb) {
-            const int s = kb % kStages;
-            ok = mbar_wait(&full[s], (kb / kStages) & 1, 3);
-            if (!ok) break;
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // MMA issuer: tile t accumulates into accumulator t & 1
+            const uint32_t idesc = instr_desc(BF16, args.bn);
+            int64_t it = 0, t = 0;
+            bool ok = true;
+            for (int64_t w = blockIdx.x; w < work && ok; w += gridDim.x, ++t) {
+                const int b = (int)(t & 1);
+                if (t >= 2 && !(ok = mbar_wait(&acc_empty[b], (uint32_t)((t >> 1) - 1) & 1, 5, abort)))
+                    break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t dacc = tmem + (uint32_t)b * acc_cols;
+                for (int kb = 0; kb < kb_n; ++kb, ++it) {
+                    const int s = (int)(it % kStages);
+                    if (!(ok = mbar_wait(&full[s], (uint32_t)(it / kStages) & 1, 3, abort))) break;
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint64_t ad = smem_desc(smem_u32(sa + s * a_bytes));
+                    const uint64_t bd = smem_desc(smem_u32(sb + s * b_bytes));
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)  // 4 MMAs of 32 bytes of K per 128-byte slice
+                        mma<BF16>(dacc, ad + kk * 2, bd + kk * 2, idesc, (kb | kk) != 0);
+                    mma_commit(&empty[s]);
+                }
+                if (ok) mma_commit(&acc_full[b]);
+            }
+            // every MMA issued above has completed before the memory is freed
+            mma_commit(mma_done);
+            mbar_wait(mma_done, 0, 6, nullptr);
+        }
+    } else {
+        // epilogue: warp w reads TMEM lanes [32 (w % 4), 32 (w % 4) + 32)
+        const int q = warp & 3;
+        int64_t t = 0;
+        for (int64_t w = blockIdx.x; w < work; w += gridDim.x, ++t) {
+            const int b = (int)(t & 1);
+            if (!mbar_wait(&acc_full[b], (uint32_t)(t >> 1) & 1, 4, abort)) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint64_t ad = smem_desc(smem_u32(sa + s * a_bytes));
-            const uint64_t bd = smem_desc(smem_u32(sb + s * b_bytes));
+            int64_t rel, row0, row_end;
+            tile_rows(args, w / args.nbn, rel, row0, row_end);
+            const int32_t col0 = (int32_t)(w % args.nbn) * args.bn;
+            const int64_t row = row0 + q * 32 + lane;
+            const bool live = row < row_end;
+            const int64_t orow = live ? (args.perm ? (int64_t)args.perm[row] : row) : 0;
+            const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)b * acc_cols;
+            // 32 columns at a time: each thread writes its row's 32 values into
+            // the warp's staging rows (16-byte chunks XOR-swizzled by row, so
+            // neither side conflicts on banks), then the warp stores whole
+            // 128-byte (64-byte bf16) row segments, 4 (8) rows per instruction
+            constexpr int CPR = BF16 ? 4 : 8;  // 16-byte chunks per staged row
+            constexpr int RPP = 32 / CPR;       // rows per store instruction
+            uint4 *stg = staging + q * 32 * 8;
+            for (int c = 0; c < args.bn; c += 32) {
+                uint32_t v[32];
+                tmem_ld16(taddr + (uint32_t)c, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+                tmem_ld16(taddr + (uint32_t)c + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
+                tmem_wait_ld();
+                if (BF16) {
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk)  // 4 MMAs of 32 bytes of K per 128-byte slice
-                mma<BF16>(tmem, ad + kk * 2, bd + kk * 2, idesc, (kb | kk) != 0);
-            mma_commit(&empty[s]);
-        }
-        mma_commit(accum);  // arrives once everything issued above has completed
-    }
-    __syncwarp();
-
-    // epilogue: all four warps, warp w reads TMEM lanes [32w, 32w + 32)
-    const bool ready = mbar_wait(accum, 0, 4);
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const int64_t row = row0 + warp * 32 + lane;
-    const bool live = ready && row < row_end;
-    const int64_t orow = live ? (args.perm ? (int64_t)args.perm[row] : row) : 0;
-    const int32_t col0 = nb * args.bn;
-    for (int c = 0; c < args.bn; c += 8) {
-        uint32_t v[8];
-        tmem_ld8(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c, v);
-        const int32_t col = col0 + c;
-        if (!live || col >= args.d2) continue;
-        if (BF16) {
-            __nv_bfloat16 *o = static_cast<__nv_bfloat16 *>(args.out) + orow * args.d2 + col;
-            __align__(16) __nv_bfloat16 h[8];
+                    for (int j = 0; j < 4; ++j) {
+                        uint32_t w[4];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) h[i] = __float2bfloat16_rn(__uint_as_float(v[i]));
-            *reinterpret_cast<uint4 *>(o) = *reinterpret_cast<const uint4 *>(h);
-        } else {
-            float *o = static_cast<float *>(args.out) + orow * args.d2 + col;
-            reinterpret_cast<float4 *>(o)[0] =
-                make_float4(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2]),
-                            __uint_as_float(v[3]));
-            reinterpret_cast<float4 *>(o)[1] =
-                make_float4(__uint_as_float(v[4]), __uint_as_float(v[5]), __uint_as_float(v[6]),
-                            __uint_as_float(v[7]));
+                        for (int i = 0; i < 4; ++i) {
+                            __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(v[8 * j + 2 * i]),
+                                                                     __uint_as_float(v[8 * j + 2 * i + 1]));
+                            w[i] = *reinterpret_cast<uint32_t *>(&h);
+                        }
+                        stg[lane * 8 + (j ^ (lane & 3))] = make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        stg[lane * 8 + (j ^ (lane & 7))] =
+                            make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                }
+                __syncwarp();
+#pragma unroll
+                for (int pass = 0; pass < 32 / RPP; ++pass) {
+                    const int rr = pass * RPP + lane / CPR, j = lane % CPR;
+                    const int64_t orr = __shfl_sync(0xffffffffu, orow, rr);
+                    const bool lr = __shfl_sync(0xffffffffu, live, rr);
+                    const int32_t col = col0 + c + j * (BF16 ? 8 : 4);  // first column of the chunk
+                    const uint4 x = stg[rr * 8 + (j ^ (rr & (CPR - 1)))];
+                    if (lr && col < args.d2) {  // d2 is a multiple of 8: chunks are whole
+                        if (BF16)
+                            *reinterpret_cast<uint4 *>(static_cast<__nv_bfloat16 *>(args.out) +
+                                                       orr * args.d2 + col) = x;
+                        else
+                            *reinterpret_cast<uint4 *>(static_cast<float *>(args.out) + orr * args.d2 +
+                                                       col) = x;
+                    }
+                }
+                __syncwarp();
+            }
+            // this warp is done reading accumulator b
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[b]);
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -266,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (warp == 1) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                     "r"(tmem_cols));
+                     "r"(2 * acc_cols));
     }
 }
 
@@ -346,7 +438,8 @@ int make_map(CUtensorMap *map, const void *ptr, int bf16, int64_t inner, int64_t
 }
 
 size_t smem_bytes(int bn) {
-    return 1024 + kStages * (size_t(kBM) * 128 + size_t(bn) * 128) + 8 * (2 * kStages + 1) + 16;
+    return 1024 + kStages * (size_t(kBM) * 128 + size_t(bn) * 128) + 4 * 32 * kStageRowBytes +
+           8 * (2 * kStages + 5) + 16;
 }
 
 }  // namespace
@@ -420,9 +513,12 @@ int gmm_tensor_core(const void *a, const void *b, void *out, const GmmLayout &l,
     args.d2 = (int32_t)d2;
     args.bn = bn;
     args.kb = (int32_t)((d1 + bk - 1) / bk);
+    args.nbn = (int32_t)((d2 + bn - 1) / bn);
     const size_t smem = smem_bytes(bn);
-    int64_t max_tiles = (n + kBM - 1) / kBM + r;
-    dim3 grid((unsigned)max_tiles, (unsigned)((d2 + bn - 1) / bn));
+    // persistent: one CTA per SM (its 4-stage ring and 2 x BN TMEM columns),
+    // never more CTAs than (row tile, column tile) pairs could exist
+    int64_t max_work = ((n + kBM - 1) / kBM + r) * args.nbn;
+    dim3 grid((unsigned)(max_work < num_sms() ? max_work : num_sms()));
     if (bf16) {
         BGL_CUDA(cudaFuncSetAttribute(k_gmm_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)smem));

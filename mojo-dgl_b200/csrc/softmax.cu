@@ -308,14 +308,16 @@ __global__ void __launch_bounds__(kSoftBlock) k_softmax_stats(const SoftArgs<T> 
 // in CSR order, the gSpMM way: logits come through the same per-lane cp.async
 // ring (groups of UN items, P groups ahead) and every value takes one online
 // (max, sum) update -- a larger value rescales the running sum.
+// Both cases need exp(-|z - m|): a larger z rescales the running sum by
+// exp(m - z) and adds 1, a smaller one adds exp(z - m).  One exponential per
+// value and a select, no divergent branch.
 template <typename T>
 __device__ __forceinline__ void online(T &m, T &s, T z) {
-    if (z > m) {
-        s = Arith<T>::add(Arith<T>::mul(s, Arith<T>::ex(Arith<T>::sub(m, z))), T(1));
-        m = z;
-    } else {
-        s = Arith<T>::add(s, Arith<T>::ex(Arith<T>::sub(z, m)));
-    }
+    const T dz = Arith<T>::sub(z, m);
+    const T e = Arith<T>::ex(dz > T(0) ? -dz : dz);
+    const bool up = z > m;
+    s = up ? Arith<T>::add(Arith<T>::mul(s, e), T(1)) : Arith<T>::add(s, e);
+    m = up ? z : m;
 }
 
 constexpr int kWalkUN = 4;     // items per group

@@ -74,7 +74,10 @@ def edge_softmax(graph, logits, eids=ALL, norm_by="dst"):
             indptr = torch.zeros(1, dtype=torch.int64, device=key.device)
         num_rows, num_items = int(indptr.numel()) - 1, k
         lt = T.to_dev(logits, dtype).reshape(out_len, d)[:k].contiguous()
-    out = torch.zeros((out_len, d), dtype=dtype, device=T.device())
+    # every selected item is written; rows past the selection stay zero
+    out = torch.empty((out_len, d), dtype=dtype, device=T.device())
+    if k is not None and k < out_len:
+        out[k:].zero_()
     if num_rows and num_items and d:
         nbytes = lib().bgl_softmax_workspace_size(num_rows, num_items, d, T.code_of(dtype))
         ws = T.workspace(nbytes)

@@ -89,7 +89,8 @@ def segment_softmax(seglen, value):
     feat, d = flat_feature(value)
     num_seg = int(offsets.numel()) - 1
     dtype = T.common_float(value)
-    out = torch.zeros((n, d), dtype=dtype, device=T.device())
+    # every row of value belongs to one segment and is written
+    out = torch.empty((n, d), dtype=dtype, device=T.device())
     if num_seg and n and d:
         vt = T.to_dev(value, dtype)
         nbytes = lib().bgl_softmax_workspace_size(num_seg, n, d, T.code_of(dtype))
@@ -132,7 +133,8 @@ def segment_mm(a, b, seglen_a):
         if lo < 0 or total > n:
             raise DGLError("segment lengths must be non-negative and sum to {}, got a minimum of "
                            "{} and a sum of {}".format(n, lo, total))
-    out = torch.zeros((n, d2), dtype=dtype, device=T.device())
+    # the library writes every row (rows past sum(seglen_a) as zeros)
+    out = torch.empty((n, d2), dtype=dtype, device=T.device())
     if n:
         at, bt, st = T.to_dev(a, dtype), T.to_dev(b, dtype), T.to_dev(seg)
         code = T.code_of(dtype)
