@@ -12,9 +12,11 @@ and copy_u_sum are timed beside it under "ops".
 
 Multi-GPU (torchrun, one rank per GPU): strong scaling of the same graph,
 destination rows partitioned by in-edge count, features owned in equal row
-blocks.  A step passes the feature blocks around a ring of NCCL send/recv
-steps and runs one accumulating gSpMM pass over the rank's edges from each
-block's owner as the block arrives, so the halo overlaps the aggregation;
+blocks.  A step gathers the feature blocks slice by slice (each owner block
+cut into HALO_SLICES row slices, one NCCL all-gather per slice) and runs one
+accumulating gSpMM pass over the rank's edges whose sources fall in a slice as
+soon as it is in, while the next slice is gathered, so the halo overlaps the
+aggregation;
 "allgather_then_compute" times the unpipelined alternative (one all-gather,
 then the local gSpMM) and "compute_only" the local gSpMM alone.
 
@@ -44,6 +46,7 @@ CFG3 = dict(num_nodes=2_500_000, num_edges=125_000_000, dim=128, seed=3)
 METRIC = "gSpMM Gedge-feat/s"
 UNIT = "Gedge-feat/s"
 CPU_SAMPLE_EDGES = 1 << 23
+HALO_SLICES = 4  # feature slices of the multi-GPU halo (one all-gather + one gSpMM pass each)
 
 
 # ----------------------------------------------------------------- workload
@@ -240,7 +243,7 @@ def run_ours(args):
 
     import mojodgl as dgl
     from mojodgl import ops
-    from mojodgl.partition import (DeviceShard, DstShard, OwnerPipeline, edge_balanced_ranges,
+    from mojodgl.partition import (DeviceShard, DstShard, SlicePipeline, edge_balanced_ranges,
                                    owner_blocks)
 
     rank, world, local = dist_env()
@@ -261,18 +264,20 @@ def run_ours(args):
     bounds = edge_balanced_ranges(indeg, world)
     lo, hi = int(bounds[rank]), int(bounds[rank + 1])
     shard = DeviceShard(DstShard(u, v, lo, hi))
-    pipe = OwnerPipeline(u, v, lo, hi, rank, world, n) if world > 1 else None
+    pipe = SlicePipeline(u, v, lo, hi, rank, world, n, slices=HALO_SLICES) if world > 1 else None
     blk, owners = owner_blocks(n, world)
     own_lo, own_hi = owners[rank]
     h_dev = torch.from_numpy(h).to(dev)  # full features (kernel-only timing)
     gathered = torch.empty((blk * world, d), dtype=torch.float32, device=dev)
-    my_block = torch.zeros((blk, d), dtype=torch.float32, device=dev)
+    # this rank's owner block, padded to whole slices for the sliced gather
+    my_block = torch.zeros((pipe.block_rows() if pipe else blk, d), dtype=torch.float32, device=dev)
     my_block[: own_hi - own_lo] = h_dev[own_lo:own_hi]
     out = torch.empty((hi - lo, d), dtype=torch.float32, device=dev)
     ws = None
     torch.cuda.synchronize()
 
-    bufs = [torch.empty_like(my_block), torch.empty_like(my_block)] if world > 1 else None
+    bufs = ([torch.empty((world * pipe.sb, d), dtype=torch.float32, device=dev) for _ in range(2)]
+            if world > 1 else None)
     pws = [None]
 
     def step():
@@ -284,7 +289,7 @@ def run_ours(args):
             shard.copy_u(h_dev, "mean", out=out, workspace=ws)
 
     def step_allgather():
-        dist.all_gather_into_tensor(gathered, my_block)
+        dist.all_gather_into_tensor(gathered, my_block[:blk])
         shard.copy_u(gathered, "mean", out=out, workspace=ws)
 
     def timed(fn, steps, warmup):
@@ -374,7 +379,7 @@ def run_ours(args):
         e2e = {"value": e_total * d / dt / 1e9, "unit": UNIT,
                "h2d_bytes_per_step": int(h.nbytes), "d2h_bytes_per_step": int(n * d * 4),
                "ms_per_step": dt * 1e3,
-               "path": "per rank: pinned h block H2D, ring halo overlapped with gSpMM passes, "
+               "path": "per rank: pinned h block H2D, sliced all-gather halo overlapped with gSpMM passes, "
                        "output rows D2H"}
 
     # -------- roofline of the dominant kernel (this rank's gSpMM)
@@ -416,7 +421,7 @@ def run_ours(args):
                                    "cfg3 copy_u_mean with edges scaled by {} (profiling case)"
                                    .format(args.scale),
                        "num_nodes": n, "num_edges": e_total, "dim": d, "seed": c["seed"],
-                       "parallelism": "dst-row shards x{} + owner-pipelined NCCL ring halo".format(world)
+                       "parallelism": "dst-row shards x{} + sliced all-gather halo overlapped with gSpMM passes".format(world)
                        if world > 1 else "single GPU",
                        "l2": "inputs larger than L2 (h 1.28 GB, indices 0.5 GB)"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,

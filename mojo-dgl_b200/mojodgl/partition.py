@@ -4,11 +4,14 @@ Every output row of gSpMM is independent (the reference splits its 32 CPU
 workers the same way, src/ported.mojo:34-39, 442-443), so the graph is cut
 into P contiguous destination-row ranges with about E/P in-edges each (a
 row-count split would not balance a power-law in-degree).  Node features are
-owned in P contiguous, equal row blocks; before an aggregation every rank
-gathers the full feature matrix with one NCCL all-gather (the halo: with
-uniform sources a shard references nearly every source row, so a selective
-exchange would not pay), then runs gSpMM on its own rows.  Outputs stay
-sharded by destination row.
+owned in P contiguous, equal row blocks.  With uniform sources a shard
+references nearly every source row, so the halo is the whole feature matrix
+and a selective exchange would not pay.  DeviceShard runs the local gSpMM on
+a gathered matrix (one all-gather, then compute); SlicePipeline overlaps the
+two, gathering the blocks slice by slice with one all-gather each and running
+an accumulating gSpMM pass per slice as it arrives (OwnerPipeline does the
+same over a ring of point-to-point steps, one owner block per step).
+Outputs stay sharded by destination row.
 
 The host logic here (ranges, shard extraction, block layout) is plain numpy
 and is tested with gloo ranks on CPU; the kernels run through mojodgl.
@@ -238,3 +241,125 @@ def ring_exchange(my_block, bufs, rank, world, on_block):
         if k + 1 < P:
             works = issue(k + 1)
         on_block((r - k) % P, bufs[k % 2], False, k == P - 1)
+
+
+def slice_rows(blk: int, slices: int):
+    """Rows per slice when each owner block of `blk` rows is cut into
+    `slices` equal slices (the last may hold fewer real rows)."""
+    return max(1, -(-blk // slices))
+
+
+def slice_of(u: np.ndarray, blk: int, sb: int):
+    """For global source rows u: the slice they fall in and their row in
+    that slice's gathered buffer (owners concatenated in rank order, sb rows
+    each)."""
+    owner = u // blk
+    off = u - owner * blk
+    c = off // sb
+    return c, owner * sb + (off - c * sb)
+
+
+class SlicePipeline:
+    """A destination-row shard whose in-edges are split by the slice of
+    their source's owner block, so the halo exchange overlaps the
+    aggregation with collectives rather than point-to-point steps.
+
+    Every owner block of features is cut into C equal row slices.  Step c
+    gathers slice c of every rank's block with one NCCL all-gather (the
+    collective runs at the all-gather bus rate; NCCL's point-to-point
+    send/recv moved a third of that in the same box) and runs one gSpMM pass
+    over the shard's edges whose sources fall in those slices, while the
+    gather of slice c + 1 is in flight.  Passes after the first fold into the
+    output (BGL_ACCUMULATE); the mean divide and the max/min inf->0 run on
+    the last pass.  The sub-CSRs keep global edge ids, so max/min ties
+    resolve to the smaller edge id, as in the single-GPU result; sums add
+    the same messages slice by slice (compared with a tolerance against the
+    single-GPU order)."""
+
+    def __init__(self, u, v, lo, hi, rank, world, num_nodes, slices=4):
+        import torch
+
+        from . import _tensor as T
+        from ._lib import check, lib
+
+        self.rank, self.world = rank, world
+        self.lo, self.hi = int(lo), int(hi)
+        self.blk, self.owners = owner_blocks(num_nodes, world)
+        self.slices = int(slices)
+        self.sb = slice_rows(self.blk, self.slices)
+        n = self.hi - self.lo
+        sel = np.nonzero((v >= lo) & (v < hi))[0]
+        vv = v[sel] - lo
+        cc, local = slice_of(u[sel], self.blk, self.sb)
+        dev = T.device()
+        self.parts = []
+        for c in range(self.slices):
+            m = np.nonzero(cc == c)[0]
+            ne = int(m.size)
+            key = torch.from_numpy(np.ascontiguousarray(vv[m])).to(dev)
+            other = torch.from_numpy(np.ascontiguousarray(local[m])).to(dev)
+            indptr = torch.empty(n + 1, dtype=torch.int64, device=dev)
+            deg = torch.empty(n, dtype=torch.int64, device=dev)
+            order = torch.empty(ne, dtype=torch.int32, device=dev)
+            indices = torch.empty(ne, dtype=torch.int32, device=dev)
+            nbytes = lib().bgl_csr_build_workspace_size(ne, n)
+            ws = T.workspace(nbytes)
+            check(lib().bgl_csr_build(T.ptr(key), T.ptr(other), ne, n, T.ptr(indptr), T.ptr(deg),
+                                      T.ptr(order), T.ptr(indices), T.ptr(ws), nbytes, T.stream()),
+                  "bgl_csr_build")
+            gid = torch.from_numpy(sel[m].astype(np.int64)).to(dev)
+            eid = gid[order.long()].to(torch.int32) if ne else order
+            self.parts.append((indptr, indices, eid, ne))
+        self.deg = torch.from_numpy(np.bincount(vv, minlength=n).astype(np.int64)).to(dev)
+        self.num_rows = n
+
+    def block_rows(self):
+        """Rows of the (padded) feature block each rank contributes."""
+        return self.slices * self.sb
+
+    # the pass is the owner pipeline's: same accumulate / last-pass rules
+    _pass = OwnerPipeline._pass
+
+    def copy_u(self, my_block, reduce_op, out, arg_e=None, bufs=None, ws=None):
+        """out[rows of this shard] = reduce over in-edges of the source
+        feature; my_block is this rank's (block_rows(), D) feature block."""
+        ws = ws if ws is not None else [None]
+
+        def on_slice(c, gathered, first, last):
+            self._pass(c, gathered, out, reduce_op, first, last, arg_e, ws)
+
+        slice_exchange(my_block, self.sb, self.slices, self.world, bufs, on_slice)
+        return out
+
+
+def slice_exchange(my_block, sb, slices, world, bufs, on_slice):
+    """Hand on_slice(c, gathered, first, last) every slice c of all ranks'
+    blocks, gathered rank-major (world * sb rows), gathering slice c + 1
+    while slice c is processed; the two buffers alternate, and a buffer is
+    refilled only after the work queued on it (a collective is ordered after
+    the work already on the current stream).  NCCL gathers into one tensor
+    asynchronously; other backends (gloo, for the CPU tests) gather a list
+    and copy it in."""
+    import torch
+    import torch.distributed as dist
+
+    if bufs is None:
+        bufs = [my_block.new_empty((world * sb,) + tuple(my_block.shape[1:])) for _ in range(2)]
+    nccl = dist.get_backend() == "nccl"
+
+    def issue(c):
+        part = my_block[c * sb:(c + 1) * sb]
+        if nccl:
+            return dist.all_gather_into_tensor(bufs[c % 2], part, async_op=True)
+        pieces = [torch.empty_like(part) for _ in range(world)]
+        dist.all_gather(pieces, part.contiguous())
+        torch.cat(pieces, out=bufs[c % 2])
+        return None
+
+    work = issue(0)
+    for c in range(slices):
+        if work is not None:
+            work.wait()
+        if c + 1 < slices:
+            work = issue(c + 1)
+        on_slice(c, bufs[c % 2], c == 0, c == slices - 1)

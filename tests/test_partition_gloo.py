@@ -171,3 +171,82 @@ def test_ring_halo_reproduces_the_single_process_result(world):
         np.testing.assert_allclose(sums, want_sum[lo:hi], rtol=1e-12, atol=1e-12)
         np.testing.assert_array_equal(best, want_max[lo:hi])
         np.testing.assert_array_equal(best_e, want_e[lo:hi])
+
+
+def _slice_rank(rank, world, port, q, slices):
+    """The sliced-gather halo: slice c of every owner block arrives by one
+    all-gather and is reduced over the shard's edges whose sources fall in
+    it; sums add slice by slice, max keeps the better value with the smaller
+    edge id on a tie."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import sys
+
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        sys.path.insert(0, root)
+        from oracle import oracle as orc
+
+        from mojodgl.partition import slice_exchange, slice_of, slice_rows
+
+        u, v, h, n = graph(seed=13)
+        bounds = edge_balanced_ranges(np.bincount(v, minlength=n), world)
+        lo, hi = int(bounds[rank]), int(bounds[rank + 1])
+        blk, owners = owner_blocks(n, world)
+        sb = slice_rows(blk, slices)
+        a, b = owners[rank]
+        mine = torch.zeros(slices * sb, h.shape[1], dtype=torch.float64)
+        mine[: b - a] = torch.from_numpy(h[a:b])
+        sel = np.nonzero((v >= lo) & (v < hi))[0]
+        cc, local = slice_of(u[sel], blk, sb)
+        sums = np.zeros((hi - lo, h.shape[1]))
+        best = np.full((hi - lo, h.shape[1]), -np.inf)
+        best_e = np.full((hi - lo, h.shape[1]), -1, dtype=np.int64)
+        seen = []
+
+        def on_slice(c, gathered, first, last):
+            seen.append((c, first, last))
+            assert gathered.shape[0] == world * sb
+            k = np.nonzero(cc == c)[0]
+            og = orc.Graph(local[k], v[sel[k]] - lo, num_nodes=max(world * sb, hi - lo))
+            x = gathered.numpy()
+            part = orc.gspmm(og, "copy_lhs", "sum", x, None)[: hi - lo]
+            sums[:] = part if first else sums + part
+            mx, au, ae = orc.gspmm(og, "copy_lhs", "max", x, None, with_arg=True)
+            mx, ae = mx[: hi - lo], ae[: hi - lo]
+            ge = np.where(ae >= 0, sel[k][np.maximum(ae, 0)], -1)  # global edge ids
+            take = (mx > best) | ((mx == best) & (ge >= 0) & ((best_e < 0) | (ge < best_e)))
+            best[take] = mx[take]
+            best_e[take] = ge[take]
+
+        slice_exchange(mine, sb, slices, world, None, on_slice)
+        q.put((rank, lo, hi, sums, best, best_e, seen))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,slices", [(2, 3), (3, 4)])
+def test_slice_halo_reproduces_the_single_process_result(world, slices):
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_slice_rank, args=(r, world, port, q, slices)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    from oracle import oracle as orc
+
+    u, v, h, n = graph(seed=13)
+    og = orc.Graph(u, v, num_nodes=n)
+    want_sum = orc.gspmm(og, "copy_lhs", "sum", h, None)
+    want_max, _, want_e = orc.gspmm(og, "copy_lhs", "max", h, None, with_arg=True)
+    for rank, lo, hi, sums, best, best_e, seen in results:
+        assert seen == [(c, c == 0, c == slices - 1) for c in range(slices)]
+        np.testing.assert_allclose(sums, want_sum[lo:hi], rtol=1e-12, atol=1e-12)
+        np.testing.assert_array_equal(best, want_max[lo:hi])
+        np.testing.assert_array_equal(best_e, want_e[lo:hi])
