@@ -61,6 +61,29 @@ class _DeviceGraph:
         self.in_csr = self._csr(v, u, ne, n, dev)
         self.out_csr = self._csr(u, v, ne, n, dev)
 
+    def in_row_slices(self, parts):
+        """The in-CSR cut into about `parts` destination-row slices holding
+        equal numbers of edges, for aggregations that copy each slice's rows
+        to the host while the next slice is computed: [(r0, r1, e0, e1,
+        indptr)] with indptr rebased to the slice's first edge.  Built once
+        per part count."""
+        cache = self.__dict__.setdefault("_row_slices", {})
+        if parts not in cache:
+            indptr = self.in_csr[0]
+            n = indptr.numel() - 1
+            ne = int(indptr[-1])
+            targets = torch.arange(1, parts, device=indptr.device, dtype=torch.int64) * ne // parts
+            cuts = torch.searchsorted(indptr, targets).clamp_(0, n).cpu().tolist()
+            bounds = sorted(set([0, n] + cuts))
+            ends = indptr[torch.tensor(bounds, device=indptr.device)].cpu().tolist()
+            slices = []
+            for k in range(len(bounds) - 1):
+                r0, r1 = bounds[k], bounds[k + 1]
+                if r1 > r0:
+                    slices.append((r0, r1, ends[k], ends[k + 1], (indptr[r0:r1 + 1] - ends[k]).contiguous()))
+            cache[parts] = slices
+        return cache[parts]
+
     @staticmethod
     def _csr(key, other, ne, n, dev):
         indptr = torch.empty(n + 1, dtype=torch.int64, device=dev)

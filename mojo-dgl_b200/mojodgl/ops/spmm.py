@@ -67,6 +67,14 @@ def _run(g, op, reduce_op, lhs_data, rhs_data, with_arg=False, zero_inf=False, c
     # which the kernel has in hand: no degree array is passed
     indptr, indices, eid, _ = csr if csr is not None else g._device().in_csr
     red = REDUCERS[reduce_op]
+    flags = BGL_ZERO_INF if zero_inf else 0
+    elem = torch.empty((), dtype=dtype).element_size()
+    if (kind != T.TORCH_CUDA and not with_arg and csr is None
+            and num_dst * dout * elem >= _OVERLAP_MIN_BYTES):
+        out = _run_host_overlapped(g, lt, lw, ldiv, rt, rw, rdiv, dout, dtype, code, red, flags)
+        shape = out_shape(num_dst, feat, rank)
+        res = out.reshape(shape)
+        return res.numpy() if kind == T.NUMPY else res
     dev = T.device()
     out = torch.empty((num_dst, dout), dtype=dtype, device=dev)
     arg_u = arg_e = None
@@ -77,8 +85,8 @@ def _run(g, op, reduce_op, lhs_data, rhs_data, with_arg=False, zero_inf=False, c
     ws = T.workspace(nbytes)
     rc = lib().bgl_gspmm(T.ptr(indptr), T.ptr(indices), T.ptr(eid), None, num_dst, num_edges,
                          T.ptr(lt), lw, ldiv, T.ptr(rt), rw, rdiv, T.ptr(out), dout, T.ptr(arg_u),
-                         T.ptr(arg_e), T.code_of(dtype), code, red,
-                         BGL_ZERO_INF if zero_inf else 0, T.ptr(ws), nbytes, T.stream())
+                         T.ptr(arg_e), T.code_of(dtype), code, red, flags, T.ptr(ws), nbytes,
+                         T.stream())
     check(rc, "gspmm")
     shape = out_shape(num_dst, feat, rank)
     res = T.result(out.reshape(shape), kind)
@@ -86,6 +94,50 @@ def _run(g, op, reduce_op, lhs_data, rhs_data, with_arg=False, zero_inf=False, c
         return res
     conv = lambda a: None if a is None else T.result(a.reshape(shape), kind)  # noqa: E731
     return res, (conv(arg_u), conv(arg_e))
+
+
+# A host-bound result of at least this size is computed in destination-row
+# slices, each slice's rows copied back while the next slice runs.
+_OVERLAP_MIN_BYTES = 64 << 20
+_OVERLAP_SLICES = 8
+_copy_streams = {}
+
+
+def _run_host_overlapped(g, lt, lw, ldiv, rt, rw, rdiv, dout, dtype, code, red, flags):
+    """gSpMM over the graph's in-CSR in edge-balanced destination-row slices
+    (every slice holds all in-edges of its rows, so its rows are final when
+    its launch ends); the copy of slice k's rows into pinned host memory
+    runs on a second stream while slice k + 1 is computed.  Returns the
+    pinned host result."""
+    dg = g._device()
+    dev = T.device()
+    num_dst = g.number_of_nodes()
+    _, indices, eid, _ = dg.in_csr
+    out = torch.empty((num_dst, dout), dtype=dtype, device=dev)
+    host = torch.empty((num_dst, dout), dtype=dtype, pin_memory=True)
+    slices = dg.in_row_slices(_OVERLAP_SLICES)
+    dcode = T.code_of(dtype)
+    nbytes = max(lib().bgl_gspmm_workspace_size(r1 - r0, e1 - e0, dout, dcode, red)
+                 for r0, r1, e0, e1, _ in slices)
+    ws = T.workspace(nbytes)
+    compute = torch.cuda.current_stream()
+    copier = _copy_streams.get(dev.index)
+    if copier is None:
+        copier = _copy_streams[dev.index] = torch.cuda.Stream(device=dev)
+    row_bytes = dout * out.element_size()
+    for r0, r1, e0, e1, ip in slices:
+        rc = lib().bgl_gspmm(T.ptr(ip), T.ptr(indices) + 4 * e0, T.ptr(eid) + 4 * e0, None, r1 - r0,
+                             e1 - e0, T.ptr(lt), lw, ldiv, T.ptr(rt), rw, rdiv,
+                             T.ptr(out) + r0 * row_bytes, dout, None, None, dcode, code, red, flags,
+                             T.ptr(ws), nbytes, compute.cuda_stream)
+        check(rc, "gspmm")
+        done = torch.cuda.Event()
+        done.record(compute)
+        copier.wait_event(done)
+        with torch.cuda.stream(copier):
+            host[r0:r1].copy_(out[r0:r1], non_blocking=True)
+    copier.synchronize()  # every slice's kernel and copy are done
+    return host
 
 
 def gspmm(g, op, reduce_op, lhs_data, rhs_data):

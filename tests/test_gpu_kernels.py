@@ -204,6 +204,31 @@ def test_float32_mean_is_the_correctly_rounded_sum_over_degree(split, request):
     np.testing.assert_array_equal(m, want)
 
 
+def test_host_result_sliced_path_matches_device_path():
+    """A host-bound result of 64 MB or more is computed in destination-row
+    slices whose rows are copied back while the next slice runs; it must
+    match the device-resident call: max/min bit for bit, sum/mean within the
+    float32 gSpMM bound (a hub row may be split at other chunk boundaries)."""
+    u, v = power_law(200_000, 91, mean_deg=8)
+    rng = np.random.default_rng(92)
+    x = rng.normal(size=(200_000, 128)).astype(np.float32)
+    w = rng.normal(size=(u.size, 128)).astype(np.float32)
+    g = dgl.graph((u, v), num_nodes=200_000)
+    xd, wd = torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda()
+    for red in ("sum", "mean", "max", "min"):
+        got = ops.gspmm(g, "copy_lhs", red, x, None)
+        assert isinstance(got, np.ndarray) and got.shape == (200_000, 128)
+        want = ops.gspmm(g, "copy_lhs", red, xd, None).cpu().numpy()
+        if red in ("max", "min"):
+            np.testing.assert_array_equal(got, want)
+        else:
+            s = ops.gspmm(g, "copy_lhs", "sum" if red == "sum" else "mean", np.abs(x), None)
+            within_s(got, want.astype(np.float64), s)
+    got = ops.gspmm(g, "mul", "max", torch.from_numpy(x), torch.from_numpy(w))
+    assert isinstance(got, torch.Tensor) and got.is_pinned()
+    np.testing.assert_array_equal(got.numpy(), ops.gspmm(g, "mul", "max", xd, wd).cpu().numpy())
+
+
 def test_head_broadcast_gat_layer(orc):
     """BASELINE config 2's pipeline at a small size: u_add_v on (N, H, 1),
     leaky_relu, edge_softmax over (E, H, 1), u_mul_e_sum of (N, H, D) by
