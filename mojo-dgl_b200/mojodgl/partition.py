@@ -68,6 +68,29 @@ class DstShard:
         return int(self.u.size)
 
 
+def segment_balanced_ranges(seglen: np.ndarray, parts: int):
+    """segment_mm across ranks: P+1 relation boundaries so each rank's
+    contiguous relations hold about the same number of rows; a relation's b
+    block lives with the rank that owns it, so no collective is needed."""
+    return edge_balanced_ranges(np.asarray(seglen, dtype=np.int64), parts)
+
+
+def row_block_ranges(n: int, parts: int):
+    """gather_mm across ranks: contiguous row blocks of a (b, at 64 x 256 x 256
+    values, is replicated or broadcast once)."""
+    return np.asarray([lo for lo, _ in owner_blocks(n, parts)[1]] + [n], dtype=np.int64)
+
+
+def scatter_edge_rows(pieces, num_edges: int):
+    """Stitch per-rank gSDDMM results into the (E, ...) output: pieces are
+    (global edge ids, rows) pairs, one per rank's destination shard."""
+    first = pieces[0][1]
+    out = np.zeros((num_edges,) + tuple(first.shape[1:]), dtype=first.dtype)
+    for eids, rows in pieces:
+        out[eids] = rows
+    return out
+
+
 def assemble_gathered(blocks, n: int):
     """Concatenate the P gathered (padded) owner blocks into the (n, ...) matrix."""
     return np.concatenate(blocks, axis=0)[:n]

@@ -250,3 +250,100 @@ def test_slice_halo_reproduces_the_single_process_result(world, slices):
         np.testing.assert_allclose(sums, want_sum[lo:hi], rtol=1e-12, atol=1e-12)
         np.testing.assert_array_equal(best, want_max[lo:hi])
         np.testing.assert_array_equal(best_e, want_e[lo:hi])
+
+
+def _other_ops_rank(rank, world, port, q):
+    """gSDDMM by destination shards (u features all-gathered), segment_mm by
+    relation ranges balanced by rows, gather_mm by row blocks (b replicated):
+    each rank runs the oracle on its part only."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import sys
+
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        sys.path.insert(0, root)
+        from oracle import oracle as orc
+
+        from mojodgl.partition import row_block_ranges, segment_balanced_ranges
+
+        # gsddmm u_dot_v and u_add_v on the destination shard's edges
+        u, v, h, n = graph(seed=21)
+        bounds = edge_balanced_ranges(np.bincount(v, minlength=n), world)
+        lo, hi = int(bounds[rank]), int(bounds[rank + 1])
+        shard = DstShard(u, v, lo, hi)
+        blk, owners = owner_blocks(n, world)
+        a, b = owners[rank]
+        mine = torch.zeros(blk, h.shape[1], dtype=torch.float64)
+        mine[: b - a] = torch.from_numpy(h[a:b])
+        parts = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(parts, mine)
+        full = assemble_gathered([p.numpy() for p in parts], n)
+        og = orc.Graph(shard.u, shard.v_local + lo, num_nodes=n)
+        dot = orc.gsddmm(og, "dot", full, full, "u", "v")
+        add = orc.gsddmm(og, "add", full, full, "u", "v")
+
+        # segment_mm by relation ranges
+        rng = np.random.default_rng(22)
+        r, d1, d2 = 7, 5, 3
+        seglen = rng.integers(0, 40, r)
+        rows = int(seglen.sum())
+        am = rng.normal(size=(rows, d1))
+        bm = rng.normal(size=(r, d1, d2))
+        rb = segment_balanced_ranges(seglen, world)
+        off = np.concatenate([[0], np.cumsum(seglen)])
+        r0, r1 = int(rb[rank]), int(rb[rank + 1])
+        seg_part = orc.segment_mm(am[off[r0]:off[r1]], bm[r0:r1], seglen[r0:r1]) if r1 > r0 else None
+
+        # gather_mm by row blocks
+        idx = rng.integers(0, r, 50)
+        ga = rng.normal(size=(50, d1))
+        gb = row_block_ranges(50, world)
+        g0, g1 = int(gb[rank]), int(gb[rank + 1])
+        gm_part = orc.gather_mm(ga[g0:g1], bm, idx[g0:g1])
+        q.put((rank, shard.eids, dot, add, (off[r0], off[r1], seg_part), (g0, g1, gm_part)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_other_ops_shard_and_stitch_to_the_single_process_result(world):
+    from mojodgl.partition import scatter_edge_rows
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_other_ops_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = sorted([q.get(timeout=120) for _ in procs], key=lambda t: t[0])
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    from oracle import oracle as orc
+
+    u, v, h, n = graph(seed=21)
+    og = orc.Graph(u, v, num_nodes=n)
+    np.testing.assert_array_equal(scatter_edge_rows([(t[1], t[2]) for t in results], u.size),
+                                  orc.gsddmm(og, "dot", h, h, "u", "v"))
+    np.testing.assert_array_equal(scatter_edge_rows([(t[1], t[3]) for t in results], u.size),
+                                  orc.gsddmm(og, "add", h, h, "u", "v"))
+    rng = np.random.default_rng(22)
+    r, d1, d2 = 7, 5, 3
+    seglen = rng.integers(0, 40, r)
+    am = rng.normal(size=(int(seglen.sum()), d1))
+    bm = rng.normal(size=(r, d1, d2))
+    want = orc.segment_mm(am, bm, seglen)
+    got = np.zeros_like(want)
+    for t in results:
+        s0, s1, part = t[4]
+        if part is not None:
+            got[s0:s1] = part
+    np.testing.assert_array_equal(got, want)
+    idx = rng.integers(0, r, 50)
+    ga = rng.normal(size=(50, d1))
+    want = orc.gather_mm(ga, bm, idx)
+    got = np.concatenate([t[5][2] for t in results])
+    np.testing.assert_array_equal(got, want)
