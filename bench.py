@@ -444,9 +444,9 @@ def run_ours(args):
 
 # ------------------------------------------------------------------- suite
 def make_cfg2(seed=2, n=1_000_000, mean=16, cap=50_000):
-    """Config 2: Zipf(2.1) in-degrees capped at 50,000, rescaled
-    to mean 16 keeping the cap, largest-remainder rounding; uniform sources;
-    edges shuffled."""
+    """Config 2: Zipf(2.1) in-degrees capped at 50,000, rescaled to mean 16
+    keeping the cap, largest-remainder rounding; uniform sources; edges
+    shuffled."""
     rng = np.random.default_rng(seed)
     x = np.minimum(rng.zipf(2.1, n), cap).astype(np.float64)
     total = mean * n
