@@ -425,7 +425,9 @@ def run_ours(args):
                        if world > 1 else "single GPU",
                        "l2": "inputs larger than L2 (h 1.28 GB, indices 0.5 GB)"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-            "gpu_launches": 3 * args.steps,
+            # per gSpMM call: coordinates, main and fixup kernels; at N > 1 one
+            # call per halo slice (the all-gathers are NCCL's kernels)
+            "gpu_launches": 3 * (HALO_SLICES if world > 1 else 1) * args.steps,
             "clocks": clocks.summary(), "ops": extra,
             "allgather_then_compute": None if ms_allgather is None else
             {"value": e_total * d / (ms_allgather * 1e-3) / 1e9, "unit": UNIT,
