@@ -164,6 +164,25 @@ int bgl_edge_softmax(const int64_t *indptr, const int32_t *eid, const int8_t *ma
                      int64_t d, int dtype, void *workspace, size_t workspace_bytes,
                      void *stream);
 
+/* ------------------------------------------------ fused GAT aggregation */
+/* One pass for the chain the reference runs as four operators on a GAT layer
+ * (python/mojodgl/ops/sddmm.py u_add_v -> the caller's leaky_relu ->
+ * ops/edge_softmax.py norm_by="dst" -> ops/spmm.py u_mul_e_sum; kernels at
+ * src/ported.mojo:204-329, 876-1080, 352-423):
+ *   s_e = leaky_relu(el[u_e, h] + er[v, h], negative_slope)
+ *   out[v, h, :] = sum_{e -> v} softmax_{e -> v}(s_e) * feat[u_e, h, :]
+ * over the in-CSR (indptr, indices = source ids).  feat is (sources, heads *
+ * head_dim), el (sources, heads), er (num_rows, heads), out (num_rows, heads *
+ * head_dim), all C-contiguous; rows without in-edges get 0.  No per-edge
+ * score or attention array is written.  Rounding differs from the unfused
+ * chain (rescaled running sums, one divide). */
+size_t bgl_gat_workspace_size(int64_t num_rows, int64_t num_edges, int64_t heads, int64_t head_dim,
+                              int dtype);
+int bgl_gat_aggregate(const int64_t *indptr, const int32_t *indices, int64_t num_rows,
+                      int64_t num_edges, const void *feat, const void *el, const void *er,
+                      int64_t heads, int64_t head_dim, double negative_slope, void *out, int dtype,
+                      void *workspace, size_t workspace_bytes, void *stream);
+
 /* --------------------------------------------------------- segment_mm */
 /* Replaces mdgl_segment_mm (src/capi.mojo:141-145 -> src/ported.mojo:773-804):
  * out[rows of segment r] = a[rows] @ b[r]; rows past sum(seglen) are zeroed.

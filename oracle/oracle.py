@@ -399,3 +399,16 @@ def update_all(g: Graph, ndata: dict, edata: dict, msg, red):
     if red in ("max", "min"):
         out = replace_inf_with_zero(out)
     return out
+
+
+def gat_aggregate(g: Graph, feat, el, er, negative_slope=0.2):
+    """The chain a GAT layer runs on the reference's operators: u_add_v
+    (ops/sddmm.py:83-170), leaky_relu (the caller's), edge_softmax norm_by dst
+    (ops/edge_softmax.py:11-173), u_mul_e_sum (ops/spmm.py:21-110)."""
+    n, h = feat.shape[0], feat.shape[1]
+    el3 = f64(el).reshape(n, h, 1)
+    er3 = f64(er).reshape(n, h, 1)
+    s = gsddmm(g, "add", el3, er3, "u", "v")
+    s = np.where(s > 0, s, negative_slope * s)
+    a = edge_softmax(g, s)
+    return gspmm(g, "mul", "sum", f64(feat), a)
