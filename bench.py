@@ -544,6 +544,14 @@ def run_suite(args):
         emit("cfg2", "gspmm u_mul_e_sum (N,8,64)x(E,8,1)", t_ms(lambda: ops.u_mul_e_sum(g, feat, att)),
              e * (2048 + 32 + 4 + 4) + n * 2048 + (n + 1) * 8, units=e * 512,
              extra={"max_in_degree": int(np.bincount(v).max())})
+        # the whole attention step fused (u_add_v, leaky_relu, edge_softmax,
+        # u_mul_e_sum): feature row, el by source and source id per edge, er
+        # and the output row per node
+        unfused = {"chain": "u_add_v + leaky_relu + edge_softmax + u_mul_e_sum",
+                   "chain_ms": t_ms(lambda: ops.u_mul_e_sum(g, feat, ops.edge_softmax(
+                       g, torch.nn.functional.leaky_relu(ops.u_add_v(g, el, er), 0.2))))}
+        emit("cfg2", "gat_aggregate fused (N,8,64)", t_ms(lambda: ops.gat_aggregate(g, feat, el, er)),
+             e * (2048 + 32 + 4) + n * (2048 + 32) + (n + 1) * 8, units=e * 512, extra=unfused)
         del g, el, er, feat, s, a, att
         torch.cuda.empty_cache()
     if "cfg3" in want:
