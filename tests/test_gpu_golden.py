@@ -211,6 +211,40 @@ def test_update_all_udfs_and_pull(golden):
     np.testing.assert_array_equal(g.ndata["h"], golden["fn/pull_udf/h"])
 
 
+def test_udfs_on_device_tensors(golden):
+    """The UDF paths with the graph and its features as CUDA tensors: the
+    message and reduce functions see device tensors, nothing leaves the
+    device, and the results equal the reference's (float64, bit for bit)."""
+    import torch
+
+    dev = torch.device("cuda", 0)
+
+    def pair():
+        g = dgl.graph((torch.from_numpy(golden["fn/u"]).to(dev), torch.from_numpy(golden["fn/v"]).to(dev)))
+        g.ndata["x"] = torch.from_numpy(golden["fn/x"]).to(dev)
+        g.edata["e"] = torch.from_numpy(golden["fn/e"]).to(dev)
+        return g
+
+    seen = []
+
+    def msg(edges):
+        seen.append(edges.src["x"].device)
+        return {"m": edges.src["x"] * edges.data["e"] + 1.0}
+
+    g = pair()
+    g.update_all(msg, fn.mean("m", "h"))
+    h = g.ndata["h"]
+    assert isinstance(h, torch.Tensor) and h.is_cuda and seen[-1].type == "cuda"
+    np.testing.assert_array_equal(h.cpu().numpy(), golden["fn/udf_msg_mean/h"])
+    g = pair()
+    g.update_all(fn.u_mul_e("x", "e", "m"), lambda nodes: {"h": nodes.mailbox["m"] * 2.0})
+    assert g.ndata["h"].is_cuda
+    np.testing.assert_array_equal(g.ndata["h"].cpu().numpy(), golden["fn/udf_reduce/h"])
+    g = pair()
+    g.pull(torch.from_numpy(golden["fn/pull/targets"]).to(dev), msg, fn.mean("m", "h"))
+    np.testing.assert_array_equal(g.ndata["h"].cpu().numpy(), golden["fn/pull_udf/h"])
+
+
 def test_zero_degree_rows(golden):
     g = dgl.graph((golden["zero/u"], golden["zero/v"]), num_nodes=5)
     x, e = golden["zero/x"], golden["zero/e"]
