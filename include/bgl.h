@@ -163,6 +163,15 @@ int bgl_edge_softmax(const int64_t *indptr, const int32_t *eid, const int8_t *ma
                      int64_t num_rows, int64_t num_items, const void *logits, void *out,
                      int64_t d, int dtype, void *workspace, size_t workspace_bytes,
                      void *stream);
+/* bgl_edge_softmax over every edge (no mask), given the row of every edge by
+ * edge id (edge_row[e]: the destination of edge e for norm_by "dst", its
+ * source for "src"; eid must permute [0, num_items)).  With it the output
+ * pass runs in edge order -- logits read and outputs written contiguously --
+ * for rows of up to 8 column vectors.  Same workspace as bgl_edge_softmax. */
+int bgl_edge_softmax_by_edge(const int64_t *indptr, const int32_t *eid, const int32_t *edge_row,
+                             int64_t num_rows, int64_t num_items, const void *logits, void *out,
+                             int64_t d, int dtype, void *workspace, size_t workspace_bytes,
+                             void *stream);
 
 /* ------------------------------------------------ fused GAT aggregation */
 /* One pass for the chain the reference runs as four operators on a GAT layer

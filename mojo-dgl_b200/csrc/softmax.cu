@@ -53,6 +53,7 @@ struct SoftArgs {
     T *head_m, *head_s, *tail_m, *tail_s;  // per chunk x d: the split rows' (max, sum) pieces
     T *row_m, *row_r;                      // per row x d: each row's max and 1 / sum
     int32_t *item_row;                     // per item: its row
+    const int32_t *edge_row;               // optional: the row of every edge, by edge id
 };
 
 // (m, s) <- the softmax statistics of the items of (m, s) followed by those of
@@ -608,6 +609,54 @@ __global__ void __launch_bounds__(kSoftBlock) k_softmax_apply(const SoftArgs<T> 
     }
 }
 
+// Pass 2 in edge order, when the caller supplies every edge's row
+// (edge_row, indexed by edge id; eid then permutes [0, num_items)): logits
+// are read and outputs written contiguously, and the rows' statistics --
+// small for narrow rows -- are the gathered side.
+template <typename T, int V, int CV>
+__global__ void __launch_bounds__(kSoftBlock) k_softmax_apply_edges(const SoftArgs<T> a) {
+    constexpr int UN = 4;
+    const int c = (threadIdx.x & 31) % CV;
+    const int64_t team = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) / CV;
+    const int64_t teams = ((int64_t)gridDim.x * blockDim.x) / CV;
+    const int32_t cvn = a.d / V;
+    const int64_t d = a.d;
+    for (int32_t cb = 0; cb < cvn; cb += CV) {
+        const int32_t cv = cb + c;
+        if (cv >= cvn) break;
+        const int64_t col = (int64_t)cv * V;
+        for (int64_t e0 = team; e0 < a.num_items; e0 += teams * UN) {
+            int32_t r[UN];
+            bool ok[UN];
+#pragma unroll
+            for (int u = 0; u < UN; ++u) {
+                const int64_t e = e0 + u * teams;
+                ok[u] = e < a.num_items;
+                if (ok[u]) r[u] = __ldg(a.edge_row + e);
+            }
+            T z[UN][V], m[UN][V], rr[UN][V];
+#pragma unroll
+            for (int u = 0; u < UN; ++u) {
+                if (ok[u]) {
+                    ld_stream(a.logits + (e0 + u * teams) * d + col, z[u]);
+                    load_vec<T, V>(a.row_m + (int64_t)r[u] * d + col, m[u]);
+                    load_vec<T, V>(a.row_r + (int64_t)r[u] * d + col, rr[u]);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < UN; ++u) {
+                if (ok[u]) {
+                    T o[V];
+#pragma unroll
+                    for (int v = 0; v < V; ++v)
+                        o[v] = Arith<T>::mul(Arith<T>::ex(Arith<T>::sub(z[u][v], m[u][v])), rr[u][v]);
+                    store_vec<T, V>(a.out + (e0 + u * teams) * d + col, o);
+                }
+            }
+        }
+    }
+}
+
 struct SoftPlan {
     int vmax;  // widest vector the row width allows
     int64_t num_chunks, items, split_min;
@@ -683,7 +732,10 @@ int launch_softmax(const SoftArgs<T> &a, cudaStream_t s) {
     const int64_t cap = int64_t(num_sms()) * 2048 / CV * 2;
     if (teams > cap) teams = cap;
     const int agrid = (int)((teams * CV + kSoftBlock - 1) / kSoftBlock);
-    k_softmax_apply<T, V, CV><<<agrid < 1 ? 1 : agrid, kSoftBlock, 0, s>>>(a);
+    if (a.edge_row)
+        k_softmax_apply_edges<T, V, CV><<<agrid < 1 ? 1 : agrid, kSoftBlock, 0, s>>>(a);
+    else
+        k_softmax_apply<T, V, CV><<<agrid < 1 ? 1 : agrid, kSoftBlock, 0, s>>>(a);
     BGL_LAUNCH_CHECK();
     return BGL_OK;
 }
@@ -725,7 +777,7 @@ int launch_by_cv(const SoftArgs<T> &a, int cv, cudaStream_t s) {
 template <typename T>
 int run_softmax(const int64_t *indptr, const int32_t *eid, const int8_t *mask, int64_t rows,
                 int64_t items, const void *logits, void *out, int64_t d, int dtype, void *ws,
-                cudaStream_t s) {
+                cudaStream_t s, const int32_t *edge_row = nullptr) {
     SoftPlan p = softmax_plan(rows, items, d, dtype);
     SoftLayout<T> l = softmax_layout<T>(ws, p, rows, items, d);
     constexpr int VM = sizeof(T) == 4 ? 4 : 2;
@@ -736,7 +788,7 @@ int run_softmax(const int64_t *indptr, const int32_t *eid, const int8_t *mask, i
     SoftArgs<T> a{indptr,   eid,        mask,       (int32_t)rows, (int32_t)items,
                   (const T *)logits, (T *)out, (int32_t)d, p.num_chunks, l.coords,
                   l.head_row, l.tail_row, l.head_m, l.head_s,      l.tail_m,
-                  l.tail_s, l.row_m,    l.row_r,    l.item_row};
+                  l.tail_s, l.row_m,    l.row_r,    l.item_row, edge_row};
     int cg = (int)((p.num_chunks + 1 + 255) / 256);
     k_spmm_coords<<<cg, 256, 0, s>>>(indptr, rows, items, p.items, p.split_min, p.num_chunks,
                                      l.coords);
@@ -780,6 +832,31 @@ int bgl_edge_softmax(const int64_t *indptr, const int32_t *eid, const int8_t *ma
                                   workspace, s);
     return run_softmax<double>(indptr, eid, mask, num_rows, num_items, logits, out, d, dtype,
                                workspace, s);
+}
+
+int bgl_edge_softmax_by_edge(const int64_t *indptr, const int32_t *eid, const int32_t *edge_row,
+                             int64_t num_rows, int64_t num_items, const void *logits, void *out,
+                             int64_t d, int dtype, void *workspace, size_t workspace_bytes,
+                             void *stream) {
+    if (!edge_row) return fail(BGL_E_INVALID, "bgl_edge_softmax_by_edge: null edge_row");
+    if (dtype != BGL_F32 && dtype != BGL_F64)
+        return fail(BGL_E_UNSUPPORTED, "bgl_edge_softmax_by_edge: dtype %d (f32 and f64 only)", dtype);
+    if (num_rows < 0 || num_items < 0 || d < 0)
+        return fail(BGL_E_INVALID, "bgl_edge_softmax_by_edge: negative size");
+    if (num_rows >= (int64_t(1) << 31) || num_items >= (int64_t(1) << 31) || d >= (int64_t(1) << 31))
+        return fail(BGL_E_UNSUPPORTED, "bgl_edge_softmax_by_edge: sizes must be below 2^31");
+    if (num_rows == 0 || num_items == 0 || d == 0) return BGL_OK;
+    if (!indptr || !logits || !out) return fail(BGL_E_INVALID, "bgl_edge_softmax_by_edge: null buffer");
+    const size_t need = softmax_ws(num_rows, num_items, d, dtype);
+    if (workspace_bytes < need || !workspace)
+        return fail(BGL_E_WORKSPACE, "bgl_edge_softmax_by_edge: workspace %zu < %zu bytes",
+                    workspace_bytes, need);
+    cudaStream_t s = as_stream(stream);
+    if (dtype == BGL_F32)
+        return run_softmax<float>(indptr, eid, nullptr, num_rows, num_items, logits, out, d, dtype,
+                                  workspace, s, edge_row);
+    return run_softmax<double>(indptr, eid, nullptr, num_rows, num_items, logits, out, d, dtype,
+                               workspace, s, edge_row);
 }
 
 }  // extern "C"

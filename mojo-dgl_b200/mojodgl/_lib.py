@@ -54,6 +54,7 @@ SIGNATURES = {
                     _INT, _INT, _P], _INT),
     "bgl_softmax_workspace_size": ([_I64, _I64, _I64, _INT], _SZ),
     "bgl_edge_softmax": ([_P, _P, _P, _I64, _I64, _P, _P, _I64, _INT, _P, _SZ, _P], _INT),
+    "bgl_edge_softmax_by_edge": ([_P, _P, _P, _I64, _I64, _P, _P, _I64, _INT, _P, _SZ, _P], _INT),
     "bgl_gat_workspace_size": ([_I64, _I64, _I64, _I64, _INT], _SZ),
     "bgl_gat_aggregate": ([_P, _P, _I64, _I64, _P, _P, _P, _I64, _I64, ctypes.c_double, _P, _INT,
                            _P, _SZ, _P], _INT),

@@ -52,6 +52,7 @@ def edge_softmax(graph, logits, eids=ALL, norm_by="dst"):
             raise DGLError("logits has {} rows but the graph has {} edges".format(out_len, num_edges))
         indptr, _, eid, _ = dg.in_csr if norm_by == "dst" else dg.out_csr
         num_rows, num_items, k = graph.number_of_nodes(), num_edges, None
+        edge_row = dg.v32 if norm_by == "dst" else dg.u32  # every edge's row, by edge id
         lt = T.to_dev(logits, dtype).reshape(out_len, d)
     else:
         order = T.ids(eids)
@@ -73,6 +74,7 @@ def edge_softmax(graph, logits, eids=ALL, norm_by="dst"):
         else:
             indptr = torch.zeros(1, dtype=torch.int64, device=key.device)
         num_rows, num_items = int(indptr.numel()) - 1, k
+        edge_row = None
         lt = T.to_dev(logits, dtype).reshape(out_len, d)[:k].contiguous()
     # every selected item is written; rows past the selection stay zero
     out = torch.empty((out_len, d), dtype=dtype, device=T.device())
@@ -81,8 +83,13 @@ def edge_softmax(graph, logits, eids=ALL, norm_by="dst"):
     if num_rows and num_items and d:
         nbytes = lib().bgl_softmax_workspace_size(num_rows, num_items, d, T.code_of(dtype))
         ws = T.workspace(nbytes)
-        rc = lib().bgl_edge_softmax(T.ptr(indptr), T.ptr(eid), None, num_rows, num_items,
-                                    T.ptr(lt), T.ptr(out), d, T.code_of(dtype), T.ptr(ws), nbytes,
-                                    T.stream())
+        if edge_row is not None:
+            rc = lib().bgl_edge_softmax_by_edge(T.ptr(indptr), T.ptr(eid), T.ptr(edge_row),
+                                                num_rows, num_items, T.ptr(lt), T.ptr(out), d,
+                                                T.code_of(dtype), T.ptr(ws), nbytes, T.stream())
+        else:
+            rc = lib().bgl_edge_softmax(T.ptr(indptr), T.ptr(eid), None, num_rows, num_items,
+                                        T.ptr(lt), T.ptr(out), d, T.code_of(dtype), T.ptr(ws),
+                                        nbytes, T.stream())
         check(rc, "edge_softmax")
     return T.result(out.reshape(shape), kind)
