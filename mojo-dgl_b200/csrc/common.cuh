@@ -141,6 +141,31 @@ __device__ __forceinline__ void store_vec(T *p, const T (&r)[V]) {
     *reinterpret_cast<VT *>(p) = v;
 }
 
+// Streaming (evict-first) variants for data touched once -- the per-edge
+// outputs of gSDDMM and the softmax, the edge-order softmax's logits -- so
+// that L2 keeps the small per-node arrays those kernels gather again (CUDA's
+// __stcs / __ldcs cache-streaming operators; config 2's u_add_v: 0.57 ->
+// 0.51 ms).  Index and edge-id streams stay on the default path (a team reads
+// consecutive ids from one line, and L1 serves all but the first), and so do
+// the gSpMM and GAT row outputs, which measured no better or slower with it.
+template <typename T, int V>
+__device__ __forceinline__ void store_stream(T *p, const T (&r)[V]) {
+    using VT = typename VecT<T, V>::type;
+    VT v;
+    T *s = reinterpret_cast<T *>(&v);
+#pragma unroll
+    for (int i = 0; i < V; ++i) s[i] = r[i];
+    __stcs(reinterpret_cast<VT *>(p), v);
+}
+template <typename T, int V>
+__device__ __forceinline__ void load_once(const T *p, T (&r)[V]) {
+    using VT = typename VecT<T, V>::type;
+    const VT v = __ldcs(reinterpret_cast<const VT *>(p));
+    const T *s = reinterpret_cast<const T *>(&v);
+#pragma unroll
+    for (int i = 0; i < V; ++i) r[i] = s[i];
+}
+
 // One operand's view: row stride `width`, output column k reads column
 // (k / div) % width.  `full` (width == dout, div == 1) is the fast path.
 template <typename T>

@@ -135,7 +135,7 @@ __global__ void __launch_bounds__(256, BGL_SDDMM_MINB) k_sddmm(const SddmmArgs<T
 #pragma unroll
                     for (int i = 0; i < V; ++i)
                         o[i] = message<OP, T>(NEED_L ? l[u][i] : T(0), NEED_R ? r[u][i] : T(0));
-                    store_vec<T, V>(a.out + (e0 + u * teams) * a.dout + k0, o);
+                    store_stream<T, V>(a.out + (e0 + u * teams) * a.dout + k0, o);
                 }
             }
         }

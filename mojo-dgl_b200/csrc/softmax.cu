@@ -283,7 +283,7 @@ __global__ void __launch_bounds__(kSoftBlock) k_softmax_stats(const SoftArgs<T> 
             }
             carry_row = lrend > wend ? lrow : -1;
             x = lrow;
-            if (cb == 0 && valid && c == 0) a.item_row[i] = row;
+            if (cb == 0 && valid && c == 0) __stcs(a.item_row + i, row);
             fstage = fstage + 1 == R ? 0 : fstage + 1;
             cstage = cstage + 1 == R ? 0 : cstage + 1;
         }
@@ -529,7 +529,7 @@ __global__ void __launch_bounds__(kSoftBlock, 3) k_softmax_walk_apply(const Soft
 #pragma unroll
             for (int v = 0; v < V; ++v)
                 o[v] = Arith<T>::mul(Arith<T>::ex(Arith<T>::sub(z[v], m[v])), r[v]);
-            store_vec<T, V>(a.out + (int64_t)e * d + col, o);
+            store_stream<T, V>(a.out + (int64_t)e * d + col, o);
         });
     }
 }
@@ -602,7 +602,7 @@ __global__ void __launch_bounds__(kSoftBlock) k_softmax_apply(const SoftArgs<T> 
 #pragma unroll
                     for (int v = 0; v < V; ++v)
                         o[v] = Arith<T>::mul(Arith<T>::ex(Arith<T>::sub(z[u][v], m[u][v])), rr[u][v]);
-                    store_vec<T, V>(a.out + e[u] * d + col, o);
+                    store_stream<T, V>(a.out + e[u] * d + col, o);
                 }
             }
         }
@@ -638,7 +638,7 @@ __global__ void __launch_bounds__(kSoftBlock) k_softmax_apply_edges(const SoftAr
 #pragma unroll
             for (int u = 0; u < UN; ++u) {
                 if (ok[u]) {
-                    ld_stream(a.logits + (e0 + u * teams) * d + col, z[u]);
+                    load_once<T, V>(a.logits + (e0 + u * teams) * d + col, z[u]);
                     load_vec<T, V>(a.row_m + (int64_t)r[u] * d + col, m[u]);
                     load_vec<T, V>(a.row_r + (int64_t)r[u] * d + col, rr[u]);
                 }
@@ -650,7 +650,7 @@ __global__ void __launch_bounds__(kSoftBlock) k_softmax_apply_edges(const SoftAr
 #pragma unroll
                     for (int v = 0; v < V; ++v)
                         o[v] = Arith<T>::mul(Arith<T>::ex(Arith<T>::sub(z[u][v], m[u][v])), rr[u][v]);
-                    store_vec<T, V>(a.out + (e0 + u * teams) * d + col, o);
+                    store_stream<T, V>(a.out + (e0 + u * teams) * d + col, o);
                 }
             }
         }
