@@ -37,8 +37,15 @@ int by_reduce(const SpmmArgs<T> &a, int red, cudaStream_t s) {
     switch (red) {
     case BGL_RED_SUM: return launch_one<T, OP, BGL_RED_SUM, V, J>(a, s);
     case BGL_RED_MEAN: return launch_one<T, OP, BGL_RED_MEAN, V, J>(a, s);
-    case BGL_RED_MAX: return launch_one<T, OP, BGL_RED_MAX, V, J>(a, s);
-    case BGL_RED_MIN: return launch_one<T, OP, BGL_RED_MIN, V, J>(a, s);
+    // values only (no arg output, no accumulation): no winning positions
+    case BGL_RED_MAX:
+        if (!a.arg_u && !a.arg_e && !a.accumulate)
+            return launch_kernels<T, OP, kRedMaxValue, V, J, false>(a, s);
+        return launch_one<T, OP, BGL_RED_MAX, V, J>(a, s);
+    case BGL_RED_MIN:
+        if (!a.arg_u && !a.arg_e && !a.accumulate)
+            return launch_kernels<T, OP, kRedMinValue, V, J, false>(a, s);
+        return launch_one<T, OP, BGL_RED_MIN, V, J>(a, s);
     }
     return fail(BGL_E_INVALID, "gspmm: reduce code %d", red);
 }

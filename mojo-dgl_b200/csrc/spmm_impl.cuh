@@ -86,10 +86,14 @@ static __global__ void k_spmm_coords(const int64_t *__restrict__ indptr, int64_t
     }
 }
 
+// Max / min computed for their values only (no arg output asked for): the
+// same comparisons without the winning position, one select per value.
+constexpr int kRedMaxValue = 16, kRedMinValue = 17;
+
 template <int RED, typename T>
 __device__ __forceinline__ T identity() {
-    if (RED == BGL_RED_MAX) return Arith<T>::ninf();
-    if (RED == BGL_RED_MIN) return Arith<T>::pinf();
+    if (RED == BGL_RED_MAX || RED == kRedMaxValue) return Arith<T>::ninf();
+    if (RED == BGL_RED_MIN || RED == kRedMinValue) return Arith<T>::pinf();
     return T(0);
 }
 
@@ -100,6 +104,10 @@ __device__ __forceinline__ void fold(T &acc, int32_t &pos, T m, int32_t p) {
         if (m > acc) { acc = m; pos = p; }
     } else if (RED == BGL_RED_MIN) {
         if (m < acc) { acc = m; pos = p; }
+    } else if (RED == kRedMaxValue) {
+        acc = m > acc ? m : acc;
+    } else if (RED == kRedMinValue) {
+        acc = m < acc ? m : acc;
     } else {
             acc = Arith<T>::add(acc, m);
     }
@@ -176,6 +184,10 @@ __device__ __forceinline__ void emit_row(const SpmmArgs<T> &a, int64_t row, int6
                         const bool better = RED == BGL_RED_MAX ? v > old[i] : v < old[i];
                         take[i] = better || (v == old[i] && ae[i] >= 0 && (oe < 0 || ae[i] < oe));
                         o[i] = take[i] ? v : old[i];
+                    } else if (RED == kRedMaxValue) {
+                        o[i] = acc[j][i] > old[i] ? acc[j][i] : old[i];
+                    } else if (RED == kRedMinValue) {
+                        o[i] = acc[j][i] < old[i] ? acc[j][i] : old[i];
                     } else {
                         o[i] = Arith<T>::add(old[i], acc[j][i]);
                     }
