@@ -204,8 +204,7 @@ def run_reference(args):
         return 0
     c = CFG3
     u, v, h = make_cfg3(**c)
-    for _ in range(args.warmup):
-        pass
+    # the warm-up samples are timed like the others and dropped
     rates, threads, desc = time_oracle(u, v, h, c["num_nodes"], c["dim"], CPU_SAMPLE_EDGES,
                                        args.warmup + args.steps)
     rates = rates[args.warmup:]
