@@ -102,3 +102,25 @@ def test_grouped_mm_validation(lib):
     assert lib.bgl_segment_mm(None, None, None, None, -1, 1, 1, 1, 0, None, 0, None) == 1
     assert lib.bgl_gather_mm(None, None, None, None, 4, 2, 0, 2, 0, None, 0, None) == 1
     assert lib.bgl_segment_mm(None, None, None, None, 1, 1, 1, 1, 7, None, 0, None) == 3
+
+
+@pytest.mark.skipif(__import__("torch").cuda.is_available(), reason="checks the no-GPU behaviour")
+def test_no_cpu_fallback_without_a_device():
+    """Without a CUDA device every operator raises instead of computing on
+    the host: the product path is the B200 library or nothing."""
+    import numpy as np
+
+    import mojodgl as dgl
+    import mojodgl.ops as ops
+    from mojodgl.base import DGLError
+
+    g = dgl.graph((np.array([0, 1, 2]), np.array([1, 2, 0])))
+    x = np.ones((3, 4))
+    calls = [lambda: ops.copy_u_sum(g, x), lambda: ops.u_add_v(g, x, x),
+             lambda: ops.edge_softmax(g, np.ones((3, 1))),
+             lambda: ops.segment_reduce(np.array([1, 2]), x),
+             lambda: ops.segment_mm(x, np.ones((2, 4, 2)), np.array([1, 2])),
+             lambda: ops.gat_aggregate(g, np.ones((3, 2, 4)), np.ones((3, 2)), np.ones((3, 2)))]
+    for call in calls:
+        with pytest.raises(DGLError, match="CUDA device"):
+            call()
