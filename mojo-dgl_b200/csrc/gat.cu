@@ -216,14 +216,15 @@ __global__ void __launch_bounds__(kGatBlock) k_gat_fixup(const GatArgs<T> a) {
     if (chunk >= a.num_chunks) return;
     const int64_t row = a.head_row[chunk];
     if (row < 0) return;
-    int64_t first = chunk;
-    while (first > 0 && a.tail_row[first - 1] == row) --first;
+    const int64_t first = first_piece(a.tail_row, chunk, row, t, ts);
     const int32_t cvn = a.dout / V;
     for (int32_t cv = t; cv < cvn; cv += ts) {
         const int64_t col = (int64_t)cv * V;
         T M = Arith<T>::ninf(), S = T(0), A[V];
 #pragma unroll
         for (int i = 0; i < V; ++i) A[i] = T(0);
+        // unrolled so that several pieces' loads are in flight at once
+#pragma unroll 4
         for (int64_t q = first; q <= chunk; ++q) {
             const bool head = q == chunk;
             const int64_t off = q * a.dout + col;

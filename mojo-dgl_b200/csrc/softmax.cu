@@ -7,21 +7,24 @@
 // edge_softmax reaches the items through the CSR's edge ids; segment_softmax's
 // items are the consecutive rows of `value` (eid = identity).
 //
-// Pass 1 (k_softmax_stats): one warp per merge-path chunk of (row ends, items),
-// so a warp gets the same number of items whatever the degrees are and a
-// 50,000-edge attention hub is spread over many warps.  The warp's lanes are
-// split into W = 32 / CV items x CV column vectors: with 8 float32 columns a
-// step covers 16 items, with 128 or more one item (column blocks of 32 vectors
-// loop).  A step finds each item's row among 32 row ends held across the warp
-// (a binary search over shuffles), reduces every row's items of the step with
-// segmented warp scans -- max, broadcast, exp(z - max), sum -- and folds the
-// row left open at the end of the step into the next step.  A finished row
-// stores its (max, 1 / sum); a row split over chunks leaves a (max, sum) piece
-// per chunk, folded in CSR order by k_softmax_fixup.  The logits reach shared
-// memory through a per-lane cp.async ring several steps ahead of the fold, and
-// the pass records every item's row.
-// Pass 2 (k_softmax_apply): item-parallel, out = exp(z - max) * (1 / sum) with
-// the row the first pass recorded -- no walk, no divergence.
+// Pass 1 computes each row's (max, 1 / sum) over merge-path chunks of (row
+// ends, items), one warp per chunk, so a warp gets the same number of items
+// whatever the degrees are and a 50,000-edge attention hub is spread over
+// many warps.  Three forms by row width:
+//  * k_softmax_lane_stats, items of at most 64 bytes (8 float32 heads): each
+//    lane walks its own run of consecutive items with all columns in
+//    registers; split rows are joined by one warp scan per chunk;
+//  * k_softmax_stats, other narrow rows (up to 8 column vectors): a step of
+//    the warp covers 32 / CV items, finds each item's row among 32 row ends
+//    held across the warp and reduces every row's items with segmented scans;
+//  * k_softmax_walk_stats, wide rows: a team of lanes walks the chunk in CSR
+//    order, gSpMM-style.
+// Logits reach shared memory through per-lane cp.async rings.  A row split
+// over chunks leaves a (max, sum) piece per chunk, folded by k_softmax_fixup.
+// Pass 2 writes out = exp(z - max) * (1 / sum): in edge order when the caller
+// gives every edge's row (logits read and outputs written contiguously), else
+// item-parallel with the row the first pass recorded per item, or along the
+// same walk for wide rows.
 // The rounding differs from the reference's max-then-sum loops (a tree of
 // partial sums, a multiply by the reciprocal, CUDA's exp), so results are
 // compared with a relative tolerance (1e-12 in float64).
@@ -51,25 +54,25 @@ struct SoftArgs {
     int32_t *head_row;
     int32_t *tail_row;
     T *head_m, *head_s, *tail_m, *tail_s;  // per chunk x d: the split rows' (max, sum) pieces
-    T *row_m, *row_r;                      // per row x d: each row's max and 1 / sum
+    T *row_m, *row_r;                      // per row: its d maxima and d values of 1 / sum
     int32_t *item_row;                     // per item: its row
     const int32_t *edge_row;               // optional: the row of every edge, by edge id
+    int64_t rstride;                       // row_m / row_r elements between rows (2 d:
+                                           // a row's maxima and reciprocals side by side)
 };
 
 // (m, s) <- the softmax statistics of the items of (m, s) followed by those of
 // (m2, s2): the larger max wins and the other sum is rescaled to it.
+// One exponential and no branch: the smaller max's sum is scaled by
+// exp(-|m - m2|), which is 0 against an empty piece (max -inf) and taken as 1
+// for equal maxima (two empty pieces included).
 template <typename T>
 __device__ __forceinline__ void combine(T &m, T &s, T m2, T s2) {
-    if (m2 == Arith<T>::ninf()) return;
-    if (m == Arith<T>::ninf()) {
-        m = m2;
-        s = s2;
-    } else if (m2 > m) {
-        s = Arith<T>::add(Arith<T>::mul(s, Arith<T>::ex(Arith<T>::sub(m, m2))), s2);
-        m = m2;
-    } else {
-        s = Arith<T>::add(s, Arith<T>::mul(s2, Arith<T>::ex(Arith<T>::sub(m2, m))));
-    }
+    const T dm = Arith<T>::sub(m, m2);
+    const T e = m == m2 ? T(1) : Arith<T>::ex(dm > T(0) ? -dm : dm);
+    const bool keep = m >= m2;
+    s = keep ? Arith<T>::add(s, Arith<T>::mul(s2, e)) : Arith<T>::add(Arith<T>::mul(s, e), s2);
+    m = keep ? m : m2;
 }
 
 template <typename T, int V>
@@ -263,7 +266,7 @@ __global__ void __launch_bounds__(kSoftBlock) k_softmax_stats(const SoftArgs<T> 
                             T r[V];
 #pragma unroll
                             for (int v = 0; v < V; ++v) r[v] = Arith<T>::div(T(1), rs[v]);
-                            put2<T, V>(a.row_m, a.row_r, (int64_t)row * d + col, rm, r);
+                            put2<T, V>(a.row_m, a.row_r, (int64_t)row * a.rstride + col, rm, r);
                         }
                     } else if (wend == ye) {
                         put2<T, V>(a.tail_m, a.tail_s, chunk * d + col, rm, rs);
@@ -443,7 +446,7 @@ __global__ void __launch_bounds__(kSoftBlock, 3) k_softmax_walk_stats(const Soft
                     T r[V];
 #pragma unroll
                     for (int v = 0; v < V; ++v) r[v] = Arith<T>::div(T(1), s[v]);
-                    put2<T, V>(a.row_m, a.row_r, (int64_t)x * d + col, m, r);
+                    put2<T, V>(a.row_m, a.row_r, (int64_t)x * a.rstride + col, m, r);
                 } else {
                     put2<T, V>(a.head_m, a.head_s, chunk * d + col, m, s);
                 }
@@ -501,8 +504,8 @@ __global__ void __launch_bounds__(kSoftBlock, 3) k_softmax_walk_apply(const Soft
         T m[V], r[V], nm[V], nr[V];
         auto load_stats = [&](int32_t row, T(&mm)[V], T(&rr)[V]) {
             if (live && row < nrows) {
-                load_vec<T, V>(a.row_m + (int64_t)row * d + col, mm);
-                load_vec<T, V>(a.row_r + (int64_t)row * d + col, rr);
+                load_vec<T, V>(a.row_m + (int64_t)row * a.rstride + col, mm);
+                load_vec<T, V>(a.row_r + (int64_t)row * a.rstride + col, rr);
             }
         };
         load_stats(x, m, r);
@@ -534,7 +537,253 @@ __global__ void __launch_bounds__(kSoftBlock, 3) k_softmax_walk_apply(const Soft
     }
 }
 
-// Folds every split row's pieces in CSR order into its (max, 1 / sum).
+// ------------------------------------------------------------- narrow rows
+// Rows of at most kLaneBytes per item (8 heads of float32, say): lane j of the
+// warp takes the j-th run of K = ceil(items / 32) consecutive items of the
+// chunk and walks it in CSR order with every column in registers, one online
+// (max, sum) update per value -- no per-step row search, no scans.  The
+// logits come through a per-lane cp.async ring, P groups of U items ahead of
+// the fold, each lane's item ids one group ahead of their copies.  A row that
+// starts and ends inside the run is stored as it closes.  A run's first row,
+// if it began in an earlier run, is a head piece; its last row, if it goes on
+// past the run, a tail piece.  After the walk one segmented scan of the tails
+// over the warp's lanes joins every row split between runs: a head takes the
+// scanned tail of the lane before it.  The chunk's own head and tail pieces
+// (rows split between chunks) are left for k_softmax_fixup as in the other
+// passes.
+#ifndef BGL_SOFTMAX_LANE_BYTES
+#define BGL_SOFTMAX_LANE_BYTES 64  // widest item (d * sizeof(T)) the lane walk takes
+#endif
+constexpr int kLaneBytes = BGL_SOFTMAX_LANE_BYTES;
+
+template <typename T, int V, int NV>
+struct LaneRing {
+    static constexpr int VB = V * (int)sizeof(T);  // bytes of one cp.async
+    static constexpr int SLOT = NV * VB;           // bytes of one item
+    // about 16 items in flight per lane, at most 256 bytes of logits per lane
+    static constexpr int U = SLOT >= 64 ? 1 : SLOT >= 16 ? 2 : 4;
+    static constexpr int P = SLOT == 16 ? 4 : 3;
+    static constexpr int R = P + 1;
+    // logits [R * U][NV][thread], then the item ids [R * U][thread]
+    static constexpr int smem = R * U * kSoftBlock * (SLOT + 4);
+    // blocks per SM the registers are sized for: two for items of up to 32
+    // bytes (three, at 80 registers a thread, spilled and ran 3 % slower)
+    static constexpr int minb = SLOT > 32 ? 1 : 2;
+};
+
+template <typename T, int V, int NV>
+__global__ void __launch_bounds__(kSoftBlock, (LaneRing<T, V, NV>::minb))
+    k_softmax_lane_stats(const SoftArgs<T> a) {
+    using Ring = LaneRing<T, V, NV>;
+    constexpr int U = Ring::U, P = Ring::P, R = Ring::R, VB = Ring::VB;
+    using VT = typename VecT<T, V>::type;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    auto vslot = [](int stage, int u, int j) { return ((stage * U + u) * NV + j) * kSoftBlock; };
+    const uint32_t sbase = smem_addr(smem_raw) + threadIdx.x * VB;
+    const VT *pbase = reinterpret_cast<const VT *>(smem_raw) + threadIdx.x;
+    int32_t *ebase =
+        reinterpret_cast<int32_t *>(smem_raw + R * U * NV * kSoftBlock * VB) + threadIdx.x;
+
+    const int lane = threadIdx.x & 31;
+    const int64_t chunk = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;  // warp-uniform
+    if (chunk >= a.num_chunks) return;
+    const int32_t x0 = (int32_t)a.coords[chunk].x, y0 = (int32_t)a.coords[chunk].y;
+    const int32_t x1 = (int32_t)a.coords[chunk + 1].x, ye = (int32_t)a.coords[chunk + 1].y;
+    const int32_t nrows = a.num_rows;
+    const int64_t d = a.d;
+    const int32_t cvn = a.d / V;
+    const bool x0_before = x0 < nrows && (int32_t)a.indptr[x0] < y0;
+    const bool has_head = x0_before && x0 < x1;
+    const bool has_tail = x1 < nrows && max((int32_t)a.indptr[x1], y0) < ye;
+
+    const int32_t K = (ye - y0 + 31) >> 5;
+    const int32_t i0 = min(y0 + lane * K, ye), i1 = min(i0 + K, ye);
+
+    // the copy side of the ring
+    int32_t ids[U];
+    int32_t c_next = i0;
+    auto fetch = [&]() {
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (c_next + u < i1) ids[u] = a.eid ? __ldg(a.eid + c_next + u) : c_next + u;
+    };
+    auto copy_group = [&](int stage) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            if (c_next + u < i1) {
+#pragma unroll
+                for (int j = 0; j < NV; ++j)
+                    if (j < cvn)
+                        cp_async<VB>(sbase + vslot(stage, u, j) * VB,
+                                     a.logits + (int64_t)ids[u] * d + j * V);
+                ebase[(stage * U + u) * kSoftBlock] = ids[u];
+            }
+        }
+        cp_async_commit();  // an empty group past the run's end keeps the count
+        c_next += U;
+        fetch();
+    };
+    fetch();
+#pragma unroll
+    for (int g = 0; g < P; ++g) copy_group(g);
+
+    T m[NV][V], s[NV][V], hm[NV][V], hs[NV][V];
+    auto reset = [&]() {
+#pragma unroll
+        for (int j = 0; j < NV; ++j)
+#pragma unroll
+            for (int v = 0; v < V; ++v) {
+                m[j][v] = Arith<T>::ninf();
+                s[j][v] = T(0);
+            }
+    };
+    auto put_row = [&](int32_t row, const T (&mm)[NV][V], const T (&ss)[NV][V]) {
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            if (j >= cvn) break;
+            T r[V];
+#pragma unroll
+            for (int v = 0; v < V; ++v) r[v] = Arith<T>::div(T(1), ss[j][v]);
+            put2<T, V>(a.row_m, a.row_r, (int64_t)row * a.rstride + j * V, mm[j], r);
+        }
+    };
+    reset();
+#pragma unroll
+    for (int j = 0; j < NV; ++j)
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+            hm[j][v] = Arith<T>::ninf();
+            hs[j][v] = T(0);
+        }
+    int32_t x = x0, rb = 0, re = 0, hrow = -1, trow = -1;
+    if (i0 < i1) {
+        // the row holding item i0: the first row from x0 on that ends after it
+        int32_t lo = x0, hi = min(x1, nrows - 1);
+        while (lo < hi) {
+            const int32_t mid = lo + ((hi - lo) >> 1);
+            if ((int32_t)a.indptr[mid + 1] <= i0)
+                lo = mid + 1;
+            else
+                hi = mid;
+        }
+        x = lo;
+        rb = (int32_t)a.indptr[x];
+        re = (int32_t)a.indptr[x + 1];
+    }
+    // a row ends: stored if it began in this run, else it is the head piece
+    auto close_row = [&]() {
+        if (rb >= i0) {
+            put_row(x, m, s);
+        } else {
+            hrow = x;
+#pragma unroll
+            for (int j = 0; j < NV; ++j)
+#pragma unroll
+                for (int v = 0; v < V; ++v) {
+                    hm[j][v] = m[j][v];
+                    hs[j][v] = s[j][v];
+                }
+        }
+        reset();
+    };
+    int fstage = 0, cstage = P;
+    for (int32_t g0 = i0; g0 < i1; g0 += U) {
+        copy_group(cstage);
+        cp_async_wait<P>();  // the group at g0 has landed
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int32_t i = g0 + u;
+            if (i >= i1) break;
+            if (i >= re) {
+                close_row();
+                do {
+                    ++x;
+                    rb = re;
+                    re = (int32_t)a.indptr[x + 1];
+                } while (i >= re);
+            }
+            if (!a.edge_row) __stcs(a.item_row + i, x);
+            if (a.mask && a.mask[ebase[(fstage * U + u) * kSoftBlock]] != 1) continue;
+#pragma unroll
+            for (int j = 0; j < NV; ++j) {
+                if (j >= cvn) break;
+                const VT vv = pbase[vslot(fstage, u, j)];
+                const T *z = reinterpret_cast<const T *>(&vv);
+#pragma unroll
+                for (int v = 0; v < V; ++v) online(m[j][v], s[j][v], z[v]);
+            }
+        }
+        fstage = fstage + 1 == R ? 0 : fstage + 1;
+        cstage = cstage + 1 == R ? 0 : cstage + 1;
+    }
+    cp_async_wait<0>();
+    // the run's last row: a tail piece if it goes on past the run (the chunk's
+    // last row always counts as going on: the next chunk closes it), else it
+    // closes here
+    if (i0 < i1) {
+        if (re > i1 || x == x1)
+            trow = x;
+        else
+            close_row();
+    }
+    // segmented inclusive scan of the tail pieces over the lanes, in order
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int32_t orow = __shfl_up_sync(kFull, trow, off);
+#pragma unroll
+        for (int j = 0; j < NV; ++j)
+#pragma unroll
+            for (int v = 0; v < V; ++v) {
+                const T om = __shfl_up_sync(kFull, m[j][v], off);
+                const T os = __shfl_up_sync(kFull, s[j][v], off);
+                if (lane >= off && trow >= 0 && orow == trow) combine(m[j][v], s[j][v], om, os);
+            }
+    }
+    // a head piece takes the scanned tail of the lane before it when that
+    // lane's run ends in the same row
+    const int32_t prow = __shfl_up_sync(kFull, trow, 1);
+#pragma unroll
+    for (int j = 0; j < NV; ++j)
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+            const T pm = __shfl_up_sync(kFull, m[j][v], 1);
+            const T ps = __shfl_up_sync(kFull, s[j][v], 1);
+            if (hrow >= 0 && lane > 0 && prow == hrow) combine(hm[j][v], hs[j][v], pm, ps);
+        }
+    if (hrow >= 0) {
+        if (hrow == x0 && x0_before) {
+#pragma unroll
+            for (int j = 0; j < NV; ++j)
+                if (j < cvn) put2<T, V>(a.head_m, a.head_s, chunk * d + j * V, hm[j], hs[j]);
+        } else {
+            put_row(hrow, hm, hs);
+        }
+    }
+    // the chunk's tail piece: the scanned tail of the last lane with items
+    const int32_t last = ye > y0 ? (ye - y0 - 1) / K : -1;
+    if (lane == last && trow >= 0) {
+#pragma unroll
+        for (int j = 0; j < NV; ++j)
+            if (j < cvn) put2<T, V>(a.tail_m, a.tail_s, chunk * d + j * V, m[j], s[j]);
+    }
+    // row x0 ends here without an item in this chunk: an empty head piece
+    if (has_head && (int32_t)a.indptr[x0 + 1] <= y0) {
+        for (int64_t h = lane; h < d; h += 32) {
+            a.head_m[chunk * d + h] = Arith<T>::ninf();
+            a.head_s[chunk * d + h] = T(0);
+        }
+    }
+    if (lane == 0) {
+        a.head_row[chunk] = has_head ? x0 : -1;
+        a.tail_row[chunk] = has_tail ? x1 : -1;
+    }
+}
+
+// Folds every split row's pieces in CSR order into its (max, 1 / sum): one
+// warp per chunk in which a split row ends.  A row of few pieces is folded
+// with a lane per column, piece after piece; a row of many (an attention hub
+// over a hundred chunks or more) with a lane per piece and a warp reduction
+// per column -- whichever takes fewer dependent loads.
 template <typename T>
 __global__ void __launch_bounds__(kSoftBlock) k_softmax_fixup(const SoftArgs<T> a) {
     const int lane = threadIdx.x & 31;
@@ -542,15 +791,43 @@ __global__ void __launch_bounds__(kSoftBlock) k_softmax_fixup(const SoftArgs<T> 
     if (chunk >= a.num_chunks) return;
     const int32_t row = a.head_row[chunk];
     if (row < 0) return;
-    int64_t first = chunk;
-    while (first > 0 && a.tail_row[first - 1] == row) --first;
-    const int64_t d = a.d;
-    for (int64_t h = lane; h < d; h += 32) {
-        T m = Arith<T>::ninf(), s = T(0);
-        for (int64_t q = first; q < chunk; ++q) combine(m, s, a.tail_m[q * d + h], a.tail_s[q * d + h]);
-        combine(m, s, a.head_m[chunk * d + h], a.head_s[chunk * d + h]);
-        a.row_m[(int64_t)row * d + h] = m;
-        a.row_r[(int64_t)row * d + h] = Arith<T>::div(T(1), s);
+    const int64_t first = first_piece(a.tail_row, chunk, row, lane, 32);
+    const int64_t d = a.d, np = chunk - first + 1;
+    auto piece = [&](int64_t q, int64_t h, T &m, T &s) {
+        const bool head = q == chunk;
+        m = (head ? a.head_m : a.tail_m)[q * d + h];
+        s = (head ? a.head_s : a.tail_s)[q * d + h];
+    };
+    auto put = [&](int64_t h, T m, T s) {
+        a.row_m[(int64_t)row * a.rstride + h] = m;
+        a.row_r[(int64_t)row * a.rstride + h] = Arith<T>::div(T(1), s);
+    };
+    if ((d + 31) / 32 * np <= d * ((np + 31) / 32)) {
+        for (int64_t h = lane; h < d; h += 32) {
+            T m = Arith<T>::ninf(), s = T(0);
+#pragma unroll 4
+            for (int64_t q = first; q <= chunk; ++q) {
+                T m2, s2;
+                piece(q, h, m2, s2);
+                combine(m, s, m2, s2);
+            }
+            put(h, m, s);
+        }
+    } else {
+        for (int64_t h = 0; h < d; ++h) {
+            T m = Arith<T>::ninf(), s = T(0);
+            for (int64_t q = first + lane; q <= chunk; q += 32) {
+                T m2, s2;
+                piece(q, h, m2, s2);
+                combine(m, s, m2, s2);
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) {
+                const T m2 = __shfl_xor_sync(kFull, m, off), s2 = __shfl_xor_sync(kFull, s, off);
+                combine(m, s, m2, s2);
+            }
+            if (lane == 0) put(h, m, s);
+        }
     }
 }
 
@@ -591,8 +868,8 @@ __global__ void __launch_bounds__(kSoftBlock) k_softmax_apply(const SoftArgs<T> 
             for (int u = 0; u < UN; ++u) {
                 if (ok[u]) {
                     ld_stream(a.logits + e[u] * d + col, z[u]);
-                    load_vec<T, V>(a.row_m + (int64_t)r[u] * d + col, m[u]);
-                    load_vec<T, V>(a.row_r + (int64_t)r[u] * d + col, rr[u]);
+                    load_vec<T, V>(a.row_m + (int64_t)r[u] * a.rstride + col, m[u]);
+                    load_vec<T, V>(a.row_r + (int64_t)r[u] * a.rstride + col, rr[u]);
                 }
             }
 #pragma unroll
@@ -621,31 +898,38 @@ __global__ void __launch_bounds__(kSoftBlock) k_softmax_apply_edges(const SoftAr
     const int64_t teams = ((int64_t)gridDim.x * blockDim.x) / CV;
     const int32_t cvn = a.d / V;
     const int64_t d = a.d;
+    const int64_t step = teams * UN;
     for (int32_t cb = 0; cb < cvn; cb += CV) {
         const int32_t cv = cb + c;
         if (cv >= cvn) break;
         const int64_t col = (int64_t)cv * V;
-        for (int64_t e0 = team; e0 < a.num_items; e0 += teams * UN) {
-            int32_t r[UN];
-            bool ok[UN];
+        // the rows of the group after this one are read one iteration ahead,
+        // so a group's statistics and logits loads wait on nothing
+        int32_t r[UN], rn[UN];
+        auto rows_of = [&](int64_t e0, int32_t(&rr)[UN]) {
 #pragma unroll
             for (int u = 0; u < UN; ++u) {
                 const int64_t e = e0 + u * teams;
-                ok[u] = e < a.num_items;
-                if (ok[u]) r[u] = __ldg(a.edge_row + e);
+                rr[u] = e < a.num_items ? __ldg(a.edge_row + e) : -1;
             }
+        };
+        rows_of(team, rn);
+        for (int64_t e0 = team; e0 < a.num_items; e0 += step) {
+#pragma unroll
+            for (int u = 0; u < UN; ++u) r[u] = rn[u];
+            rows_of(e0 + step, rn);
             T z[UN][V], m[UN][V], rr[UN][V];
 #pragma unroll
             for (int u = 0; u < UN; ++u) {
-                if (ok[u]) {
+                if (r[u] >= 0) {
                     load_once<T, V>(a.logits + (e0 + u * teams) * d + col, z[u]);
-                    load_vec<T, V>(a.row_m + (int64_t)r[u] * d + col, m[u]);
-                    load_vec<T, V>(a.row_r + (int64_t)r[u] * d + col, rr[u]);
+                    load_vec<T, V>(a.row_m + (int64_t)r[u] * a.rstride + col, m[u]);
+                    load_vec<T, V>(a.row_r + (int64_t)r[u] * a.rstride + col, rr[u]);
                 }
             }
 #pragma unroll
             for (int u = 0; u < UN; ++u) {
-                if (ok[u]) {
+                if (r[u] >= 0) {
                     T o[V];
 #pragma unroll
                     for (int v = 0; v < V; ++v)
@@ -667,8 +951,11 @@ SoftPlan softmax_plan(int64_t rows, int64_t items, int64_t d, int dtype) {
     const int vm = dtype == BGL_F32 ? 4 : 2;
     p.vmax = (d % vm == 0) ? vm : 1;
     const int64_t total = rows + items;
-    // one warp per chunk, about four chunks per resident warp
-    int64_t target = int64_t(num_sms()) * 64 * 4;
+    // one warp per chunk, about four chunks per resident warp; the lane walk
+    // (items of at most kLaneBytes) takes two waves of 24 warps per SM, so
+    // each lane's run is long against the warp scan that ends it
+    const bool lane = d * (dtype == BGL_F32 ? 4 : 8) <= kLaneBytes;
+    int64_t target = int64_t(num_sms()) * (lane ? 24 * 2 : 64 * 4);
     const int64_t per_chunk = 4 * (d > 0 ? d : 1) * (dtype == BGL_F32 ? 4 : 8);
     const int64_t cap = (int64_t(256) << 20) / per_chunk;
     if (target > cap) target = cap;
@@ -702,8 +989,8 @@ SoftLayout<T> softmax_layout(void *ws, const SoftPlan &p, int64_t rows, int64_t 
     l.head_s = c.take<T>(p.num_chunks * d);
     l.tail_m = c.take<T>(p.num_chunks * d);
     l.tail_s = c.take<T>(p.num_chunks * d);
-    l.row_m = c.take<T>(rows * d);
-    l.row_r = c.take<T>(rows * d);
+    l.row_m = c.take<T>(rows * 2 * d);
+    l.row_r = l.row_m + d;
     l.item_row = c.take<int32_t>(items);
     l.bytes = c.used + 256;
     return l;
@@ -715,16 +1002,10 @@ size_t softmax_ws(int64_t rows, int64_t items, int64_t d, int dtype) {
     return softmax_layout<double>(nullptr, p, rows, items, d).bytes;
 }
 
+// After a warp-per-chunk statistics pass: the split rows' fixup, then the
+// item pass.
 template <typename T, int V, int CV>
-int launch_softmax(const SoftArgs<T> &a, cudaStream_t s) {
-    constexpr int R = BGL_SOFTMAX_DEPTH + 1;
-    constexpr int smem = R * kSoftBlock * (V * (int)sizeof(T) + 4);
-    auto ks = k_softmax_stats<T, V, CV>;
-    BGL_CUDA(cudaFuncSetAttribute(ks, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    const int64_t threads = a.num_chunks * 32;
-    const int grid = (int)((threads + kSoftBlock - 1) / kSoftBlock);
-    ks<<<grid, kSoftBlock, smem, s>>>(a);
-    BGL_LAUNCH_CHECK();
+int launch_finish(const SoftArgs<T> &a, int grid, cudaStream_t s) {
     k_softmax_fixup<T><<<grid, kSoftBlock, 0, s>>>(a);
     BGL_LAUNCH_CHECK();
     // the item pass: enough teams to fill the GPU a few times over
@@ -738,6 +1019,31 @@ int launch_softmax(const SoftArgs<T> &a, cudaStream_t s) {
         k_softmax_apply<T, V, CV><<<agrid < 1 ? 1 : agrid, kSoftBlock, 0, s>>>(a);
     BGL_LAUNCH_CHECK();
     return BGL_OK;
+}
+
+template <typename T, int V, int CV>
+int launch_softmax(const SoftArgs<T> &a, cudaStream_t s) {
+    constexpr int R = BGL_SOFTMAX_DEPTH + 1;
+    constexpr int smem = R * kSoftBlock * (V * (int)sizeof(T) + 4);
+    auto ks = k_softmax_stats<T, V, CV>;
+    BGL_CUDA(cudaFuncSetAttribute(ks, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    const int grid = (int)((a.num_chunks * 32 + kSoftBlock - 1) / kSoftBlock);
+    ks<<<grid, kSoftBlock, smem, s>>>(a);
+    BGL_LAUNCH_CHECK();
+    return launch_finish<T, V, CV>(a, grid, s);
+}
+
+template <typename T, int V, int NV>
+int launch_lane(const SoftArgs<T> &a, cudaStream_t s) {
+    constexpr int smem = LaneRing<T, V, NV>::smem;
+    auto ks = k_softmax_lane_stats<T, V, NV>;
+    BGL_CUDA(cudaFuncSetAttribute(ks, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    BGL_CUDA(cudaFuncSetAttribute(ks, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                  cudaSharedmemCarveoutMaxShared));
+    const int grid = (int)((a.num_chunks * 32 + kSoftBlock - 1) / kSoftBlock);
+    ks<<<grid, kSoftBlock, smem, s>>>(a);
+    BGL_LAUNCH_CHECK();
+    return launch_finish<T, V, NV>(a, grid, s);
 }
 
 template <typename T, int V>
@@ -760,6 +1066,24 @@ int launch_walk(const SoftArgs<T> &a, int ts, cudaStream_t s) {
     ka<<<grid, kSoftBlock, smem, s>>>(a, ts);
     BGL_LAUNCH_CHECK();
     return BGL_OK;
+}
+
+// Items of at most kLaneBytes: the lane walk, NV = the vectors a lane holds.
+template <typename T, int V>
+int launch_by_nv(const SoftArgs<T> &a, int nv, cudaStream_t s) {
+    switch (nv) {
+    case 1: return launch_lane<T, V, 1>(a, s);
+    case 2: return launch_lane<T, V, 2>(a, s);
+    case 4: return launch_lane<T, V, 4>(a, s);
+    case 8:
+        if constexpr (V * 8 * sizeof(T) <= kLaneBytes) return launch_lane<T, V, 8>(a, s);
+        break;
+    case 16:
+        if constexpr (V * 16 * sizeof(T) <= kLaneBytes) return launch_lane<T, V, 16>(a, s);
+        break;
+    default: break;
+    }
+    return fail(BGL_E_INVALID, "softmax: no lane walk for %d vectors", nv);
 }
 
 template <typename T, int V>
@@ -788,11 +1112,15 @@ int run_softmax(const int64_t *indptr, const int32_t *eid, const int8_t *mask, i
     SoftArgs<T> a{indptr,   eid,        mask,       (int32_t)rows, (int32_t)items,
                   (const T *)logits, (T *)out, (int32_t)d, p.num_chunks, l.coords,
                   l.head_row, l.tail_row, l.head_m, l.head_s,      l.tail_m,
-                  l.tail_s, l.row_m,    l.row_r,    l.item_row, edge_row};
+                  l.tail_s, l.row_m,    l.row_r,    l.item_row, edge_row, 2 * d};
     int cg = (int)((p.num_chunks + 1 + 255) / 256);
     k_spmm_coords<<<cg, 256, 0, s>>>(indptr, rows, items, p.items, p.split_min, p.num_chunks,
                                      l.coords);
     BGL_LAUNCH_CHECK();
+    if (d * (int64_t)sizeof(T) <= kLaneBytes) {
+        if (V == 1) return launch_by_nv<T, 1>(a, cv, s);
+        return launch_by_nv<T, VM>(a, cv, s);
+    }
     if (V == 1) return launch_by_cv<T, 1>(a, cv, s);
     return launch_by_cv<T, VM>(a, cv, s);
 }

@@ -445,6 +445,27 @@ __global__ void __launch_bounds__(kSpmmBlock, (Stages<T, OP, V>::minb)) k_spmm(c
     }
 }
 
+// The first of the chunks whose pieces make up split row `row`, which ends in
+// `chunk`: the chunks before it whose tail piece belongs to the row.  The
+// team (ts lanes, a power of two <= 32, all of them calling) probes ts chunks
+// per step, so a hub spread over hundreds of chunks costs a few dependent
+// loads rather than one per chunk.
+template <typename R>
+__device__ __forceinline__ int64_t first_piece(const R *__restrict__ tail_row, int64_t chunk,
+                                               int64_t row, int t, int ts) {
+    const int base = (threadIdx.x & 31) & ~(ts - 1);
+    const unsigned team = ts == 32 ? 0xffffffffu : ((1u << ts) - 1) << base;
+    int64_t first = chunk;
+    while (first > 0) {
+        const int64_t q = first - 1 - t;
+        const bool same = q >= 0 && (int64_t)tail_row[q] == row;
+        const unsigned brk = __ballot_sync(team, !same) >> base;
+        if (brk) return first - (__ffs(brk) - 1);
+        first -= ts;
+    }
+    return first;
+}
+
 // Folds the pieces of every split row in CSR order and writes the row.
 template <typename T, int RED, int V, int J, bool ACC>
 __global__ void __launch_bounds__(256) k_spmm_fixup(const SpmmArgs<T> a) {
@@ -454,8 +475,7 @@ __global__ void __launch_bounds__(256) k_spmm_fixup(const SpmmArgs<T> a) {
     if (chunk >= a.num_chunks) return;
     const int64_t row = a.head_row[chunk];
     if (row < 0) return;
-    int64_t first = chunk;
-    while (first > 0 && a.tail_row[first - 1] == row) --first;
+    const int64_t first = first_piece(a.tail_row, chunk, row, t, ts);
     const int64_t cvn = a.dout / V;
     for (int64_t cb = 0; cb < cvn; cb += (int64_t)ts * J) {
         T acc[J][V];
@@ -467,6 +487,8 @@ __global__ void __launch_bounds__(256) k_spmm_fixup(const SpmmArgs<T> a) {
                 acc[j][i] = identity<RED, T>();
                 pos[j][i] = -1;
             }
+        // unrolled so that several pieces' loads are in flight at once
+#pragma unroll 4
         for (int64_t q = first; q <= chunk; ++q) {
             const T *val = (q == chunk) ? a.head_val : a.tail_val;
             const int32_t *pz = (q == chunk) ? a.head_pos : a.tail_pos;

@@ -166,6 +166,51 @@ def test_edge_softmax_split_rows_both_paths(orc, small_chunks, dtype, heads):
         np.testing.assert_allclose(got, want, rtol=rtol, atol=1e-7 if dtype == np.float32 else 0)
 
 
+@pytest.fixture(params=[16, 100, 1000], ids=["chunk16", "chunk100", "chunk1000"])
+def chunk_items(request):
+    """Merge-path chunks of a fixed size: 16 gives the lane walk one item per
+    lane, 100 about three, 1000 about thirty-one."""
+    _lib.set_param("spmm_min_items", request.param)
+    _lib.set_param("spmm_max_chunks", 1 << 40)
+    _lib.set_param("spmm_split_min", 0)
+    yield request.param
+    _lib.set_param("spmm_min_items", 32)
+    _lib.set_param("spmm_max_chunks", 0)
+    _lib.set_param("spmm_split_min", 512)
+
+
+@pytest.mark.parametrize("dtype,heads", [(np.float32, h) for h in (1, 3, 8, 12, 16, 32)]
+                         + [(np.float64, h) for h in (1, 2, 5, 8, 16)])
+def test_narrow_softmax_runs_and_chunks(orc, chunk_items, dtype, heads):
+    """Items of at most 64 bytes take the lane walk (each lane a run of
+    consecutive items, split rows joined by a warp scan of run pieces); wider
+    narrow rows (float32 x 32, float64 x 16) the warp-wide steps.  Hubs span
+    many runs and chunks; isolated nodes leave empty rows.  Covers the three
+    callers: edge_softmax over all edges (edge-order second pass), a positional
+    subset of edge ids and segment_softmax (item-order second pass)."""
+    u, v = power_law(3000, 51)
+    u = np.concatenate([u, [2999, 2999]])  # two nodes more, one isolated
+    v = np.concatenate([v, [3001, 3001]])
+    rng = np.random.default_rng(52)
+    z = (rng.normal(size=(u.size, heads, 1)) * 3).astype(dtype)
+    g, og = dgl.graph((u, v), num_nodes=3003), orc.Graph(u, v, 3003)
+    rtol = 2e-5 if dtype == np.float32 else 1e-12
+    atol = 1e-7 if dtype == np.float32 else 0
+    for norm_by in ("dst", "src"):
+        got = ops.edge_softmax(g, z, norm_by=norm_by)
+        want = orc.edge_softmax(og, z.astype(np.float64), norm_by=norm_by)
+        np.testing.assert_allclose(got, want, rtol=rtol, atol=atol)
+    sel = rng.permutation(u.size)[: u.size // 2]
+    got = ops.edge_softmax(g, z, eids=sel)
+    want = orc.edge_softmax(og, z.astype(np.float64), eids=sel)
+    np.testing.assert_allclose(got, want, rtol=rtol, atol=atol)
+    seglen = np.bincount(v, minlength=3003)
+    val = z.reshape(u.size, heads)
+    np.testing.assert_allclose(ops.segment_softmax(seglen, val),
+                               orc.segment_softmax(seglen, val.astype(np.float64)),
+                               rtol=rtol, atol=atol)
+
+
 def test_split_rows_are_deterministic(small_chunks):
     u, v = power_law(5000, 41)
     x = np.random.default_rng(42).normal(size=(5000, 64)).astype(np.float32)
