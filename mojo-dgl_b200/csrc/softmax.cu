@@ -538,123 +538,138 @@ __global__ void __launch_bounds__(kSoftBlock, 3) k_softmax_walk_apply(const Soft
 }
 
 // ------------------------------------------------------------- narrow rows
-// Rows of at most kLaneBytes per item (8 heads of float32, say): lane j of the
-// warp takes the j-th run of K = ceil(items / 32) consecutive items of the
-// chunk and walks it in CSR order with every column in registers, one online
-// (max, sum) update per value -- no per-step row search, no scans.  The
-// logits come through a per-lane cp.async ring, P groups of U items ahead of
-// the fold, each lane's item ids one group ahead of their copies.  A row that
-// starts and ends inside the run is stored as it closes.  A run's first row,
-// if it began in an earlier run, is a head piece; its last row, if it goes on
-// past the run, a tail piece.  After the walk one segmented scan of the tails
-// over the warp's lanes joins every row split between runs: a head takes the
-// scanned tail of the lane before it.  The chunk's own head and tail pieces
-// (rows split between chunks) are left for k_softmax_fixup as in the other
-// passes.
+// Rows of at most kLaneBytes per item (8 heads of float32, say).  The warp's
+// lanes form 32 / L runs of L lanes, L = the item's column vectors, so a lane
+// holds one vector of V columns and the L lanes of a run read an item's row
+// with one instruction (one request per row: random rows cost requests, not
+// bytes).  Run j takes the j-th stretch of K = ceil(items / runs) consecutive
+// items of the chunk and walks it in CSR order, one online (max, sum) update
+// per value -- no per-step row search, no scans.  The logits come through a
+// per-lane cp.async ring, P groups of U items ahead of the fold; the edge ids
+// through shared-memory tiles the warp copies with instructions that cover
+// whole segments of a run's ids.  A row that starts and ends inside a run is
+// stored as it closes.  A run's first row, if it began in an earlier run, is
+// a head piece; its last row, if it goes on past the run, a tail piece.  After
+// the walk one segmented scan of the tails over the runs joins every row split
+// between runs: a head takes the scanned tail of the run before it.  The
+// chunk's own head and tail pieces (rows split between chunks) are left for
+// k_softmax_fixup as in the other passes.
 #ifndef BGL_SOFTMAX_LANE_BYTES
 #define BGL_SOFTMAX_LANE_BYTES 64  // widest item (d * sizeof(T)) the lane walk takes
 #endif
 constexpr int kLaneBytes = BGL_SOFTMAX_LANE_BYTES;
 
-template <typename T, int V, int NV>
+template <typename T, int V, int L>
 struct LaneRing {
-    static constexpr int VB = V * (int)sizeof(T);  // bytes of one cp.async
-    static constexpr int SLOT = NV * VB;           // bytes of one item
-    // about 16 items in flight per lane, at most 256 bytes of logits per lane
-    static constexpr int U = SLOT >= 64 ? 1 : SLOT >= 16 ? 2 : 4;
-    static constexpr int P = SLOT == 16 ? 4 : 3;
+    static constexpr int VB = V * (int)sizeof(T);  // one cp.async per lane and item
+    static constexpr int RUNS = 32 / L;            // runs per warp
+    static constexpr int U = VB >= 16 ? 2 : 4;     // items per group
+    static constexpr int P = VB >= 16 ? 4 : 3;     // groups in flight ahead of the fold
     static constexpr int R = P + 1;
-    // logits [R * U][NV][thread], then the item ids [R * U][thread]
-    static constexpr int smem = R * U * kSoftBlock * (SLOT + 4);
-    // blocks per SM the registers are sized for: two for items of up to 32
-    // bytes (three, at 80 registers a thread, spilled and ran 3 % slower)
-    static constexpr int minb = SLOT > 32 ? 1 : 2;
+    // logits [R * U][thread], then the item ids [R * U][thread]
+    static constexpr int ring_bytes = R * U * kSoftBlock * (VB + 4);
+    // then each warp's edge ids in tiles of W per run, two buffers, rows padded
+    // to S words; a tile holds GPT ring groups and is loaded one tile ahead of
+    // the copies that use it
+    static constexpr int W = 16;
+    static constexpr int GPT = W / U;
+    static constexpr int S = W + 1;
+    static constexpr int smem = ring_bytes + (kSoftBlock / 32) * 2 * RUNS * S * 4;
+    static_assert(GPT >= P + 1, "a tile must land before the copies that read it");
+    static_assert(RUNS * W % 32 == 0, "a tile is copied by whole warp instructions");
 };
 
-template <typename T, int V, int NV>
-__global__ void __launch_bounds__(kSoftBlock, (LaneRing<T, V, NV>::minb))
-    k_softmax_lane_stats(const SoftArgs<T> a) {
-    using Ring = LaneRing<T, V, NV>;
-    constexpr int U = Ring::U, P = Ring::P, R = Ring::R, VB = Ring::VB;
+template <typename T, int V, int L>
+__global__ void __launch_bounds__(kSoftBlock, 3) k_softmax_lane_stats(const SoftArgs<T> a) {
+    using Ring = LaneRing<T, V, L>;
+    constexpr int U = Ring::U, P = Ring::P, R = Ring::R, VB = Ring::VB, RUNS = Ring::RUNS;
+    constexpr int W = Ring::W, S = Ring::S, GPT = Ring::GPT;
     using VT = typename VecT<T, V>::type;
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    auto vslot = [](int stage, int u, int j) { return ((stage * U + u) * NV + j) * kSoftBlock; };
+    auto slot = [](int stage, int u) { return (stage * U + u) * kSoftBlock; };
     const uint32_t sbase = smem_addr(smem_raw) + threadIdx.x * VB;
     const VT *pbase = reinterpret_cast<const VT *>(smem_raw) + threadIdx.x;
-    int32_t *ebase =
-        reinterpret_cast<int32_t *>(smem_raw + R * U * NV * kSoftBlock * VB) + threadIdx.x;
+    int32_t *ebase = reinterpret_cast<int32_t *>(smem_raw + R * U * kSoftBlock * VB) + threadIdx.x;
 
     const int lane = threadIdx.x & 31;
+    const int run = lane / L, c = lane % L;  // the lane's run and column vector
     const int64_t chunk = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;  // warp-uniform
     if (chunk >= a.num_chunks) return;
     const int32_t x0 = (int32_t)a.coords[chunk].x, y0 = (int32_t)a.coords[chunk].y;
     const int32_t x1 = (int32_t)a.coords[chunk + 1].x, ye = (int32_t)a.coords[chunk + 1].y;
     const int32_t nrows = a.num_rows;
     const int64_t d = a.d;
-    const int32_t cvn = a.d / V;
+    const bool live = c < a.d / V;
+    const int64_t col = (int64_t)c * V;
     const bool x0_before = x0 < nrows && (int32_t)a.indptr[x0] < y0;
     const bool has_head = x0_before && x0 < x1;
     const bool has_tail = x1 < nrows && max((int32_t)a.indptr[x1], y0) < ye;
 
-    const int32_t K = (ye - y0 + 31) >> 5;
-    const int32_t i0 = min(y0 + lane * K, ye), i1 = min(i0 + K, ye);
+    const int32_t K = (ye - y0 + RUNS - 1) / RUNS;
+    const int32_t i0 = min(y0 + run * K, ye), i1 = min(i0 + K, ye);
 
-    // the copy side of the ring
-    int32_t ids[U];
-    int32_t c_next = i0;
-    auto fetch = [&]() {
+    // Edge ids: the warp copies tile q -- ids [q W, q W + W) of every run --
+    // with instructions that each cover 32 / W runs x W consecutive ids.
+    int32_t *tiles = reinterpret_cast<int32_t *>(smem_raw + Ring::ring_bytes) +
+                     (threadIdx.x >> 5) * 2 * RUNS * S;
+    const bool staged = a.eid != nullptr;  // warp-uniform
+    auto load_tile = [&](int32_t q) {
+        int32_t *t = tiles + (q & 1) * RUNS * S;
 #pragma unroll
-        for (int u = 0; u < U; ++u)
-            if (c_next + u < i1) ids[u] = a.eid ? __ldg(a.eid + c_next + u) : c_next + u;
+        for (int k = 0; k < RUNS * W / 32; ++k) {
+            const int r = k * (32 / W) + lane / W, o = lane % W;
+            const int32_t rs = min(y0 + r * K, ye), p = rs + q * W + o;
+            if (p < min(rs + K, ye)) cp_async<4>(smem_addr(t + r * S + o), a.eid + p);
+        }
     };
+    // the copy side of the ring
+    int32_t c_next = i0;
     auto copy_group = [&](int stage) {
+        const int32_t off = c_next - i0;  // a multiple of U, so the group is in one tile
+        const int32_t *t = tiles + ((off / W) & 1) * RUNS * S + run * S + off % W;
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             if (c_next + u < i1) {
-#pragma unroll
-                for (int j = 0; j < NV; ++j)
-                    if (j < cvn)
-                        cp_async<VB>(sbase + vslot(stage, u, j) * VB,
-                                     a.logits + (int64_t)ids[u] * d + j * V);
-                ebase[(stage * U + u) * kSoftBlock] = ids[u];
+                const int32_t id = staged ? t[u] : c_next + u;
+                if (live) cp_async<VB>(sbase + slot(stage, u) * VB, a.logits + (int64_t)id * d + col);
+                ebase[slot(stage, u)] = id;
             }
         }
         cp_async_commit();  // an empty group past the run's end keeps the count
         c_next += U;
-        fetch();
     };
-    fetch();
+    if (staged) {
+        load_tile(0);
+        load_tile(1);
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncwarp();
 #pragma unroll
     for (int g = 0; g < P; ++g) copy_group(g);
 
-    T m[NV][V], s[NV][V], hm[NV][V], hs[NV][V];
+    T m[V], s[V], hm[V], hs[V];
     auto reset = [&]() {
 #pragma unroll
-        for (int j = 0; j < NV; ++j)
-#pragma unroll
-            for (int v = 0; v < V; ++v) {
-                m[j][v] = Arith<T>::ninf();
-                s[j][v] = T(0);
-            }
-    };
-    auto put_row = [&](int32_t row, const T (&mm)[NV][V], const T (&ss)[NV][V]) {
-#pragma unroll
-        for (int j = 0; j < NV; ++j) {
-            if (j >= cvn) break;
-            T r[V];
-#pragma unroll
-            for (int v = 0; v < V; ++v) r[v] = Arith<T>::div(T(1), ss[j][v]);
-            put2<T, V>(a.row_m, a.row_r, (int64_t)row * a.rstride + j * V, mm[j], r);
+        for (int v = 0; v < V; ++v) {
+            m[v] = Arith<T>::ninf();
+            s[v] = T(0);
         }
+    };
+    auto put_row = [&](int32_t row, const T (&mm)[V], const T (&ss)[V]) {
+        if (!live) return;
+        T r[V];
+#pragma unroll
+        for (int v = 0; v < V; ++v) r[v] = Arith<T>::div(T(1), ss[v]);
+        store_vec<T, V>(a.row_m + (int64_t)row * a.rstride + col, mm);
+        store_vec<T, V>(a.row_r + (int64_t)row * a.rstride + col, r);
     };
     reset();
 #pragma unroll
-    for (int j = 0; j < NV; ++j)
-#pragma unroll
-        for (int v = 0; v < V; ++v) {
-            hm[j][v] = Arith<T>::ninf();
-            hs[j][v] = T(0);
-        }
+    for (int v = 0; v < V; ++v) {
+        hm[v] = Arith<T>::ninf();
+        hs[v] = T(0);
+    }
     int32_t x = x0, rb = 0, re = 0, hrow = -1, trow = -1;
     if (i0 < i1) {
         // the row holding item i0: the first row from x0 on that ends after it
@@ -677,19 +692,25 @@ __global__ void __launch_bounds__(kSoftBlock, (LaneRing<T, V, NV>::minb))
         } else {
             hrow = x;
 #pragma unroll
-            for (int j = 0; j < NV; ++j)
-#pragma unroll
-                for (int v = 0; v < V; ++v) {
-                    hm[j][v] = m[j][v];
-                    hs[j][v] = s[j][v];
-                }
+            for (int v = 0; v < V; ++v) {
+                hm[v] = m[v];
+                hs[v] = s[v];
+            }
         }
         reset();
     };
     int fstage = 0, cstage = P;
-    for (int32_t g0 = i0; g0 < i1; g0 += U) {
+    // the same number of steps on every lane (the tiles are the warp's)
+    const int32_t steps = (K + U - 1) / U;
+    for (int32_t step = 0; step < steps; ++step) {
+        // the copies of this step start a tile: the next one is loaded now,
+        // with this step's group, and has landed P steps later, before its
+        // first use GPT steps later
+        if (staged && (step + P) % GPT == 0) load_tile((step + P) / GPT + 1);
         copy_group(cstage);
-        cp_async_wait<P>();  // the group at g0 has landed
+        cp_async_wait<P>();  // the group of this step has landed
+        __syncwarp();        // and so have the other lanes' tile copies
+        const int32_t g0 = i0 + step * U;
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int32_t i = g0 + u;
@@ -702,16 +723,12 @@ __global__ void __launch_bounds__(kSoftBlock, (LaneRing<T, V, NV>::minb))
                     re = (int32_t)a.indptr[x + 1];
                 } while (i >= re);
             }
-            if (!a.edge_row) __stcs(a.item_row + i, x);
-            if (a.mask && a.mask[ebase[(fstage * U + u) * kSoftBlock]] != 1) continue;
+            if (!a.edge_row && c == 0) __stcs(a.item_row + i, x);
+            if (!live || (a.mask && a.mask[ebase[slot(fstage, u)]] != 1)) continue;
+            const VT vv = pbase[slot(fstage, u)];
+            const T *z = reinterpret_cast<const T *>(&vv);
 #pragma unroll
-            for (int j = 0; j < NV; ++j) {
-                if (j >= cvn) break;
-                const VT vv = pbase[vslot(fstage, u, j)];
-                const T *z = reinterpret_cast<const T *>(&vv);
-#pragma unroll
-                for (int v = 0; v < V; ++v) online(m[j][v], s[j][v], z[v]);
-            }
+            for (int v = 0; v < V; ++v) online(m[v], s[v], z[v]);
         }
         fstage = fstage + 1 == R ? 0 : fstage + 1;
         cstage = cstage + 1 == R ? 0 : cstage + 1;
@@ -726,45 +743,41 @@ __global__ void __launch_bounds__(kSoftBlock, (LaneRing<T, V, NV>::minb))
         else
             close_row();
     }
-    // segmented inclusive scan of the tail pieces over the lanes, in order
+    // segmented inclusive scan of the tail pieces over the runs, in order
 #pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-        const int32_t orow = __shfl_up_sync(kFull, trow, off);
-#pragma unroll
-        for (int j = 0; j < NV; ++j)
-#pragma unroll
-            for (int v = 0; v < V; ++v) {
-                const T om = __shfl_up_sync(kFull, m[j][v], off);
-                const T os = __shfl_up_sync(kFull, s[j][v], off);
-                if (lane >= off && trow >= 0 && orow == trow) combine(m[j][v], s[j][v], om, os);
-            }
-    }
-    // a head piece takes the scanned tail of the lane before it when that
-    // lane's run ends in the same row
-    const int32_t prow = __shfl_up_sync(kFull, trow, 1);
-#pragma unroll
-    for (int j = 0; j < NV; ++j)
+    for (int off = 1; off < RUNS; off <<= 1) {
+        const int32_t orow = __shfl_up_sync(kFull, trow, off * L);
 #pragma unroll
         for (int v = 0; v < V; ++v) {
-            const T pm = __shfl_up_sync(kFull, m[j][v], 1);
-            const T ps = __shfl_up_sync(kFull, s[j][v], 1);
-            if (hrow >= 0 && lane > 0 && prow == hrow) combine(hm[j][v], hs[j][v], pm, ps);
+            const T om = __shfl_up_sync(kFull, m[v], off * L);
+            const T os = __shfl_up_sync(kFull, s[v], off * L);
+            if (run >= off && trow >= 0 && orow == trow) combine(m[v], s[v], om, os);
         }
+    }
+    // a head piece takes the scanned tail of the run before it when that run
+    // ends in the same row
+    const int32_t prow = __shfl_up_sync(kFull, trow, L);
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+        const T pm = __shfl_up_sync(kFull, m[v], L);
+        const T ps = __shfl_up_sync(kFull, s[v], L);
+        if (hrow >= 0 && run > 0 && prow == hrow) combine(hm[v], hs[v], pm, ps);
+    }
     if (hrow >= 0) {
         if (hrow == x0 && x0_before) {
-#pragma unroll
-            for (int j = 0; j < NV; ++j)
-                if (j < cvn) put2<T, V>(a.head_m, a.head_s, chunk * d + j * V, hm[j], hs[j]);
+            if (live) {
+                store_vec<T, V>(a.head_m + chunk * d + col, hm);
+                store_vec<T, V>(a.head_s + chunk * d + col, hs);
+            }
         } else {
             put_row(hrow, hm, hs);
         }
     }
-    // the chunk's tail piece: the scanned tail of the last lane with items
+    // the chunk's tail piece: the scanned tail of the last run with items
     const int32_t last = ye > y0 ? (ye - y0 - 1) / K : -1;
-    if (lane == last && trow >= 0) {
-#pragma unroll
-        for (int j = 0; j < NV; ++j)
-            if (j < cvn) put2<T, V>(a.tail_m, a.tail_s, chunk * d + j * V, m[j], s[j]);
+    if (run == last && trow >= 0 && live) {
+        store_vec<T, V>(a.tail_m + chunk * d + col, m);
+        store_vec<T, V>(a.tail_s + chunk * d + col, s);
     }
     // row x0 ends here without an item in this chunk: an empty head piece
     if (has_head && (int32_t)a.indptr[x0 + 1] <= y0) {
@@ -1033,17 +1046,17 @@ int launch_softmax(const SoftArgs<T> &a, cudaStream_t s) {
     return launch_finish<T, V, CV>(a, grid, s);
 }
 
-template <typename T, int V, int NV>
+template <typename T, int V, int L>
 int launch_lane(const SoftArgs<T> &a, cudaStream_t s) {
-    constexpr int smem = LaneRing<T, V, NV>::smem;
-    auto ks = k_softmax_lane_stats<T, V, NV>;
+    constexpr int smem = LaneRing<T, V, L>::smem;
+    auto ks = k_softmax_lane_stats<T, V, L>;
     BGL_CUDA(cudaFuncSetAttribute(ks, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     BGL_CUDA(cudaFuncSetAttribute(ks, cudaFuncAttributePreferredSharedMemoryCarveout,
                                   cudaSharedmemCarveoutMaxShared));
     const int grid = (int)((a.num_chunks * 32 + kSoftBlock - 1) / kSoftBlock);
     ks<<<grid, kSoftBlock, smem, s>>>(a);
     BGL_LAUNCH_CHECK();
-    return launch_finish<T, V, NV>(a, grid, s);
+    return launch_finish<T, V, L>(a, grid, s);
 }
 
 template <typename T, int V>
@@ -1068,7 +1081,8 @@ int launch_walk(const SoftArgs<T> &a, int ts, cudaStream_t s) {
     return BGL_OK;
 }
 
-// Items of at most kLaneBytes: the lane walk, NV = the vectors a lane holds.
+// Items of at most kLaneBytes: the lane walk, nv = the item's column vectors
+// (lanes per run).
 template <typename T, int V>
 int launch_by_nv(const SoftArgs<T> &a, int nv, cudaStream_t s) {
     switch (nv) {
