@@ -276,7 +276,11 @@ struct Stages {
 // row and open the next -- so the copy pipeline never drains at a row end.
 // Row ends are handled as the group is folded, in CSR order, so the
 // arithmetic is exactly the per-row sequential fold.
-template <typename T, int OP, int RED, int V, int J, bool ACC>
+// LM / RM: the operands' column modes (lane_cols: 0 full rows, 1 a uniform
+// broadcast, 2 per element) when the launch knows them, -1 to read them at
+// run time.  A known mode folds every mode branch and slot stride of the
+// per-edge copy and read-back into constants.
+template <typename T, int OP, int RED, int V, int J, bool ACC, int LM = -1, int RM = -1>
 __global__ void __launch_bounds__(kSpmmBlock, (Stages<T, OP, V>::minb)) k_spmm(const SpmmArgs<T> a) {
     static_assert(J == 1, "the staged gather keeps one column vector per lane");
     using S = Stages<T, OP, V>;
@@ -352,10 +356,12 @@ __global__ void __launch_bounds__(kSpmmBlock, (Stages<T, OP, V>::minb)) k_spmm(c
         uint32_t lstride = S::slot, rstride = S::slot;  // bytes per slot
         if (NEED_L) {
             lc = lane_cols<T, V>(a.lhs, k0);
+            if (LM >= 0) lc.mode = LM;
             if (lc.mode == 1) lstride = sizeof(T);
         }
         if (NEED_R) {
             rc = lane_cols<T, V>(a.rhs, k0);
+            if (RM >= 0) rc.mode = RM;
             if (rc.mode == 1) rstride = sizeof(T);
         }
 
