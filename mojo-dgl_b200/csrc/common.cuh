@@ -70,6 +70,7 @@ struct Arith<float> {
     static __device__ __forceinline__ float ninf() { return -INFINITY; }
     static __device__ __forceinline__ float pinf() { return INFINITY; }
     static __device__ __forceinline__ float ex(float a) { return expf(a); }
+    static __device__ __forceinline__ float fma(float a, float b, float c) { return __fmaf_rn(a, b, c); }
 };
 
 template <>
@@ -81,6 +82,7 @@ struct Arith<double> {
     static __device__ __forceinline__ double ninf() { return -INFINITY; }
     static __device__ __forceinline__ double pinf() { return INFINITY; }
     static __device__ __forceinline__ double ex(double a) { return exp(a); }
+    static __device__ __forceinline__ double fma(double a, double b, double c) { return __fma_rn(a, b, c); }
 };
 
 // The message functor of src/ported.mojo:92-105.
@@ -207,6 +209,24 @@ __device__ __forceinline__ void cp_async(uint32_t dst, const void *src) {
     else
         asm volatile("cp.async.ca.shared.global [%0], [%1], %2;" ::"r"(dst), "l"(src), "n"(BYTES)
                      : "memory");
+}
+// Reads back a lane's slot: one shared-memory load of V values at a 32-bit
+// shared address (volatile, so it stays after the cp.async wait before it).
+__device__ __forceinline__ void lds_vec(uint32_t a, float (&r)[4]) {
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(r[0]), "=f"(r[1]), "=f"(r[2]), "=f"(r[3]) : "r"(a));
+}
+__device__ __forceinline__ void lds_vec(uint32_t a, float (&r)[2]) {
+    asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(r[0]), "=f"(r[1]) : "r"(a));
+}
+__device__ __forceinline__ void lds_vec(uint32_t a, float (&r)[1]) {
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(r[0]) : "r"(a));
+}
+__device__ __forceinline__ void lds_vec(uint32_t a, double (&r)[2]) {
+    asm volatile("ld.shared.v2.f64 {%0, %1}, [%2];" : "=d"(r[0]), "=d"(r[1]) : "r"(a));
+}
+__device__ __forceinline__ void lds_vec(uint32_t a, double (&r)[1]) {
+    asm volatile("ld.shared.f64 %0, [%1];" : "=d"(r[0]) : "r"(a));
 }
 __device__ __forceinline__ void cp_async_commit() {
     asm volatile("cp.async.commit_group;" ::: "memory");

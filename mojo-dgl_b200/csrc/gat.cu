@@ -173,24 +173,22 @@ __global__ void __launch_bounds__(kGatBlock, 3) k_gat(const GatArgs<T> a) {
             while (e >= re) close_row();
             // a lane past the row's last column folds whatever its slot holds
             // and never stores it
-            using VT = typename VecT<T, V>::type;
-            const VT fv = *reinterpret_cast<const VT *>(smem_raw + fslot(fstage));
-            const T *f = reinterpret_cast<const T *>(&fv);
-            const T el = *reinterpret_cast<const T *>(smem_raw + eslot(fstage));
-            const T z = Arith<T>::add(el, er_row);
+            T f[V], elv[1];
+            lds_vec(s0 + fslot(fstage), f);
+            lds_vec(s0 + eslot(fstage), elv);
+            const T z = Arith<T>::add(elv[0], er_row);
             const T sc = z > T(0) ? z : Arith<T>::mul(z, a.slope);
             const T d = Arith<T>::sub(sc, M);
             const T w = Arith<T>::ex(d > T(0) ? -d : d);  // exp(-|s - M|)
-            if (sc > M) {  // a new maximum: rescale what came before, enter with weight 1
-                S = Arith<T>::add(Arith<T>::mul(S, w), T(1));
+            // a new maximum rescales what came before by w and enters with
+            // weight 1; any other score enters with weight w -- selects, not
+            // a branch (the two heads of a warp would diverge)
+            const bool up = sc > M;
+            const T c1 = up ? w : T(1), c2 = up ? T(1) : w;
+            S = Arith<T>::fma(S, c1, c2);
 #pragma unroll
-                for (int i = 0; i < V; ++i) A[i] = Arith<T>::add(Arith<T>::mul(A[i], w), f[i]);
-                M = sc;
-            } else {
-                S = Arith<T>::add(S, w);
-#pragma unroll
-                for (int i = 0; i < V; ++i) A[i] = Arith<T>::add(A[i], Arith<T>::mul(w, f[i]));
-            }
+            for (int i = 0; i < V; ++i) A[i] = Arith<T>::fma(A[i], c1, Arith<T>::mul(c2, f[i]));
+            M = up ? sc : M;
             fstage = fstage + 1 == R ? 0 : fstage + 1;
             cstage = cstage + 1 == R ? 0 : cstage + 1;
         }
