@@ -557,6 +557,11 @@ __global__ void __launch_bounds__(kSoftBlock, 3) k_softmax_walk_apply(const Soft
 #ifndef BGL_SOFTMAX_LANE_BYTES
 #define BGL_SOFTMAX_LANE_BYTES 64  // widest item (d * sizeof(T)) the lane walk takes
 #endif
+#ifndef BGL_SOFTMAX_LANE_WAVES
+// waves of 24 resident warps per SM the lane walk's chunks make (config 2: one
+// wave 5 % slower, four within 2 %)
+#define BGL_SOFTMAX_LANE_WAVES 2
+#endif
 constexpr int kLaneBytes = BGL_SOFTMAX_LANE_BYTES;
 
 template <typename T, int V, int L>
@@ -903,8 +908,14 @@ __global__ void __launch_bounds__(kSoftBlock) k_softmax_apply(const SoftArgs<T> 
 // (edge_row, indexed by edge id; eid then permutes [0, num_items)): logits
 // are read and outputs written contiguously, and the rows' statistics --
 // small for narrow rows -- are the gathered side.
+#ifndef BGL_SOFTMAX_APPLY_MINB
+// blocks per SM the edge-order pass's registers are sized for: 1 lets it keep
+// two groups' rows and values in registers (128 a thread, 2 blocks per SM);
+// sized for 3 or 4 blocks it ran 2-6 % slower on config 2
+#define BGL_SOFTMAX_APPLY_MINB 1
+#endif
 template <typename T, int V, int CV>
-__global__ void __launch_bounds__(kSoftBlock) k_softmax_apply_edges(const SoftArgs<T> a) {
+__global__ void __launch_bounds__(kSoftBlock, BGL_SOFTMAX_APPLY_MINB) k_softmax_apply_edges(const SoftArgs<T> a) {
     constexpr int UN = 4;
     const int c = (threadIdx.x & 31) % CV;
     const int64_t team = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) / CV;
@@ -968,7 +979,7 @@ SoftPlan softmax_plan(int64_t rows, int64_t items, int64_t d, int dtype) {
     // (items of at most kLaneBytes) takes two waves of 24 warps per SM, so
     // each lane's run is long against the warp scan that ends it
     const bool lane = d * (dtype == BGL_F32 ? 4 : 8) <= kLaneBytes;
-    int64_t target = int64_t(num_sms()) * (lane ? 24 * 2 : 64 * 4);
+    int64_t target = int64_t(num_sms()) * (lane ? 24 * BGL_SOFTMAX_LANE_WAVES : 64 * 4);
     const int64_t per_chunk = 4 * (d > 0 ? d : 1) * (dtype == BGL_F32 ? 4 : 8);
     const int64_t cap = (int64_t(256) << 20) / per_chunk;
     if (target > cap) target = cap;
