@@ -55,9 +55,11 @@ int by_reduce(const SpmmArgs<T> &a, int red, cudaStream_t s) {
 // with those modes fixed.  Any other combination runs the general kernels.
 template <typename T, int OP, int V, int J>
 int by_modes(const SpmmArgs<T> &a, int red, cudaStream_t s) {
-    if (V > 1 && a.lhs.full) {
-        if (a.rhs.full) return by_reduce<T, OP, V, J, 0, 0>(a, red, s);
-        if (a.rhs.uniform) return by_reduce<T, OP, V, J, 0, 1>(a, red, s);
+    if constexpr (V > 1) {
+        if (a.lhs.full) {
+            if (a.rhs.full) return by_reduce<T, OP, V, J, 0, 0>(a, red, s);
+            if (a.rhs.uniform) return by_reduce<T, OP, V, J, 0, 1>(a, red, s);
+        }
     }
     return by_reduce<T, OP, V, J>(a, red, s);
 }
