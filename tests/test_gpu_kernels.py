@@ -153,8 +153,8 @@ def test_split_rows_float64_and_args(orc, small_chunks):
 @pytest.mark.parametrize("heads", [1, 8, 64, 130])
 def test_edge_softmax_split_rows_both_paths(orc, small_chunks, dtype, heads):
     """Rows split over many merge-path chunks (chunks of ~16 items), for the
-    warp-wide step kernels (narrow rows: 1 and 8 columns) and the team walk
-    (64 and 130 columns, the latter in column blocks), norm_by dst and src."""
+    lane walk (narrow rows: 1 and 8 columns) and the team walk (64 and 130
+    columns, the latter in column blocks), norm_by dst and src."""
     u, v = power_law(3000, 37)
     rng = np.random.default_rng(38)
     z = (rng.normal(size=(u.size, heads, 1)) * 3).astype(dtype)
