@@ -168,8 +168,8 @@ def test_edge_softmax_split_rows_both_paths(orc, small_chunks, dtype, heads):
 
 @pytest.fixture(params=[16, 100, 1000], ids=["chunk16", "chunk100", "chunk1000"])
 def chunk_items(request):
-    """Merge-path chunks of a fixed size: 16 gives the lane walk one item per
-    lane, 100 about three, 1000 about thirty-one."""
+    """Merge-path chunks of a fixed size: 16 gives the lane walk's runs (32 /
+    L per warp, L lanes a run) about one item each, 100 a few, 1000 dozens."""
     _lib.set_param("spmm_min_items", request.param)
     _lib.set_param("spmm_max_chunks", 1 << 40)
     _lib.set_param("spmm_split_min", 0)
@@ -182,8 +182,10 @@ def chunk_items(request):
 @pytest.mark.parametrize("dtype,heads", [(np.float32, h) for h in (1, 3, 8, 12, 16, 32)]
                          + [(np.float64, h) for h in (1, 2, 5, 8, 16)])
 def test_narrow_softmax_runs_and_chunks(orc, chunk_items, dtype, heads):
-    """Items of at most 64 bytes take the lane walk (each lane a run of
-    consecutive items, split rows joined by a warp scan of run pieces); wider
+    """Items of at most 64 bytes take the lane walk (runs of L lanes, one per
+    column vector, each run a stretch of consecutive items; split rows joined
+    by a warp scan of run pieces; widths that are not a power-of-two count of
+    vectors leave lanes idle); wider
     narrow rows (float32 x 32, float64 x 16) the warp-wide steps.  Hubs span
     many runs and chunks; isolated nodes leave empty rows.  Covers the three
     callers: edge_softmax over all edges (edge-order second pass), a positional
