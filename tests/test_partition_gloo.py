@@ -225,7 +225,7 @@ def _slice_rank(rank, world, port, q, slices):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,slices", [(2, 3), (3, 4)])
+@pytest.mark.parametrize("world,slices", [(2, 3), (3, 4), (4, 4)])
 def test_slice_halo_reproduces_the_single_process_result(world, slices):
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -306,7 +306,7 @@ def _other_ops_rank(rank, world, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("world", [2, 3, 4])
 def test_other_ops_shard_and_stitch_to_the_single_process_result(world):
     from mojodgl.partition import scatter_edge_rows
 
