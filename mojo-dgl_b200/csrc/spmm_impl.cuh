@@ -252,8 +252,9 @@ __device__ __forceinline__ void store_piece(const SpmmArgs<T> &a, T *val, int32_
 // run best with groups of 4 and 3 in flight at three blocks per SM (copy_u sum
 // 9.5 ms; groups of 2 x 6, 3 x 4, 6 x 2, or any two-block ring: 10.2-10.9 ms);
 // binary ops with single-edge groups 4 deep (u_mul_e 19.5 ms on config 3,
-// 12.1 ms on config 2; 2 x 3: 21.1 / 14.0 ms).  Re-measured on the current
-// kernels (config 3's (E,128) edge feature / config 2's head broadcast):
+// 12.1 ms on config 2; 2 x 3: 21.1 / 14.0 ms).  Re-measured on the cp.async
+// ring just before the operand modes became template constants (config 3's
+// (E,128) edge feature / config 2's head broadcast):
 // 1 x 4: 18.5 / 9.2 ms; 2 x 3: 18.4 / 9.4; 2 x 4: 19.3 / 10.1; 4 x 2: 18.8 /
 // 9.8 ms -- the choice stands.
 constexpr int kSpmmBlock = 256;
