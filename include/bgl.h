@@ -20,6 +20,17 @@
  *     an int status (BGL_OK = 0) and never synchronises the device.  Device
  *     graph arrays use int64 row pointers and int32 column/edge ids.
  *
+ *     Precondition on the native layer, as on the reference's (whose kernels
+ *     do no bounds checks either: python/mojodgl validates before each call):
+ *     every id a kernel gathers through must be in range -- gspmm/gat
+ *     `indices` below the lhs operand's row count and `eid` below the rhs
+ *     operand's, gsddmm `u`/`v` below their operands' row counts, row
+ *     pointers non-decreasing from 0 to num_edges.  The kernels read device
+ *     arrays and do not check ids against sizes they are not given; an id out
+ *     of range reads outside the operand.  The Python layer (mojodgl) checks
+ *     node ids when a graph is built, and bgl_csr_build only produces ids in
+ *     range.
+ *
  * Op, reduce and target codes are the reference's (src/ported.mojo:44-65,
  * python/mojodgl/_lib.py:66-73).
  */
@@ -125,9 +136,11 @@ int bgl_gspmm(const int64_t *indptr, const int32_t *indices, const int32_t *eid,
  * array inside the library (bgl_static_scratch_bytes()), held by every GPU
  * that loads it until exit.  Calls needing more than that fail with
  * BGL_E_INVALID.  All calls on a device share the array, so calls that may
- * overlap on the GPU race and must be serialised by the caller.  The first
- * call on each device resolves the array's address (cudaGetSymbolAddress) and
- * should come before any stream capture.  Allocates nothing. */
+ * overlap on the GPU race and must be serialised by the caller.  The array's
+ * address is resolved (cudaGetSymbolAddress) for each CUDA context the first
+ * time a call runs in it -- the device's primary context or one the caller
+ * made current -- so make that first call before any stream capture.
+ * Allocates nothing. */
 size_t bgl_static_scratch_bytes(void);
 int bgl_gspmm_static_scratch(const int64_t *indptr, const int32_t *indices, const int32_t *eid,
                              const int64_t *deg, int64_t num_rows, int64_t num_edges,

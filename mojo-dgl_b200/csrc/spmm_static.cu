@@ -22,11 +22,16 @@
 //    at zero, because every word a call reads was written earlier in the same
 //    call (chunk boundaries by the boundary kernel, row ids and pieces by the
 //    main kernel);
-//  * the first call on each device resolves the array's device address with
-//    cudaGetSymbolAddress while that device is current (this also loads the
-//    module if it is not loaded yet); make that first call before any stream
-//    capture.
+//  * the array's device address belongs to one CUDA context: it is resolved
+//    with cudaGetSymbolAddress the first time a call runs in a context (the
+//    device's primary context, or one the caller created and made current)
+//    and cached under that context's unique id, so a context created later,
+//    also after a cudaDeviceReset, resolves its own address.  The resolving
+//    call may load the module; make the first call in each context before
+//    any stream capture.
 // Nothing here calls cudaMalloc, cudaFree or an allocating library routine.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -38,24 +43,89 @@ constexpr size_t kStaticScratchBytes = size_t(64) << 20;
 
 static __device__ __align__(256) unsigned char g_spmm_scratch[kStaticScratchBytes];
 
-std::mutex g_scratch_mutex;
-void *g_scratch_ptr[64] = {nullptr};
+// Driver entry points, fetched through the runtime (no link against the
+// driver library): the current context and its process-unique id.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext *);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long *);
 
-// The array's device address on the current device (resolved once per device).
-int scratch_address(void **out) {
-    int dev = 0;
-    BGL_CUDA(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64) return fail(BGL_E_UNSUPPORTED, "device ordinal %d out of range", dev);
-    std::lock_guard<std::mutex> lock(g_scratch_mutex);
-    if (g_scratch_ptr[dev] == nullptr) {
+struct CtxFns {
+    CtxGetCurrentFn current = nullptr;
+    CtxGetIdFn id = nullptr;
+};
+
+const CtxFns &ctx_fns() {
+    static CtxFns f;
+    static std::once_flag once;
+    std::call_once(once, [] {
         void *p = nullptr;
-        cudaError_t e = cudaGetSymbolAddress(&p, g_spmm_scratch);
-        if (e != cudaSuccess || p == nullptr)
-            return fail(BGL_E_CUDA, "cudaGetSymbolAddress(static gspmm scratch) failed: %s",
-                        cudaGetErrorString(e));
-        g_scratch_ptr[dev] = p;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            f.current = reinterpret_cast<CtxGetCurrentFn>(p);
+        p = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            f.id = reinterpret_cast<CtxGetIdFn>(p);
+    });
+    return f;
+}
+
+// Resolved addresses by context id.  A context id is never reused within a
+// process, so an entry can go stale only by its context being destroyed, and
+// then no call can run in it again; the table evicts round robin when full.
+constexpr int kSlots = 64;
+struct Slot {
+    bool used = false;
+    unsigned long long ctx_id = 0;
+    void *ptr = nullptr;
+};
+std::mutex g_scratch_mutex;
+Slot g_slots[kSlots];
+int g_next_slot = 0;
+
+// The calling thread's current context's id; *have = false if no context is
+// current.
+int current_ctx_id(bool *have, unsigned long long *id) {
+    const CtxFns &f = ctx_fns();
+    if (!f.current || !f.id)
+        return fail(BGL_E_CUDA, "cuCtxGetCurrent/cuCtxGetId are not available from the driver");
+    CUcontext ctx = nullptr;
+    *have = false;
+    if (f.current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return BGL_OK;
+    if (f.id(ctx, id) != CUDA_SUCCESS) return fail(BGL_E_CUDA, "cuCtxGetId failed");
+    *have = true;
+    return BGL_OK;
+}
+
+// The array's device address in the calling thread's current context.
+int scratch_address(void **out) {
+    bool have = false;
+    unsigned long long id = 0;
+    int rc = current_ctx_id(&have, &id);
+    if (rc != BGL_OK) return rc;
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    if (have)
+        for (const Slot &s : g_slots)
+            if (s.used && s.ctx_id == id) {
+                *out = s.ptr;
+                return BGL_OK;
+            }
+    // Not resolved in this context yet (or no context is current, in which
+    // case the runtime binds the device's primary context here).
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_spmm_scratch);
+    if (e != cudaSuccess || p == nullptr)
+        return fail(BGL_E_CUDA, "cudaGetSymbolAddress(static gspmm scratch) failed: %s",
+                    cudaGetErrorString(e));
+    if (!have) {
+        rc = current_ctx_id(&have, &id);
+        if (rc != BGL_OK) return rc;
     }
-    *out = g_scratch_ptr[dev];
+    if (have) {
+        g_slots[g_next_slot] = Slot{true, id, p};
+        g_next_slot = (g_next_slot + 1) % kSlots;
+    }
+    *out = p;
     return BGL_OK;
 }
 

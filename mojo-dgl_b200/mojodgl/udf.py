@@ -1,14 +1,20 @@
-"""Feature stores and the batches handed to user-defined functions.
+"""Feature stores and the batch objects handed to user-defined functions.
 
-Same names and behaviour as the reference's python/mojodgl/udf.py (itself
-DGL's ``dgl/udf.py``): ``g.ndata``/``g.edata`` map a field name to a
-row-per-node / row-per-edge array, and UDFs receive ``EdgeBatch`` /
-``NodeBatch`` views.  Arrays keep the caller's kind: numpy stays on the host,
-torch CUDA tensors stay resident on the device, and float32 stays float32
-(the reference converts everything to float64 on assignment, udf.py:18-26).
+Public surface as DGL's ``dgl/udf.py`` defines it, which the reference's
+python/mojodgl/udf.py also follows: ``g.ndata`` / ``g.edata`` map a field name
+to an array with one row per node / edge; a message UDF receives an
+``EdgeBatch`` (``edges.src[f]``, ``edges.dst[f]``, ``edges.data[f]``) and a
+reduce or apply UDF a ``NodeBatch`` (``nodes.mailbox[f]``, ``nodes.data[f]``,
+``nodes[f]``).
+
+Arrays keep the caller's kind: numpy arrays stay on the host and torch CUDA
+tensors stay resident on the device, and float32 stays float32 (the reference
+widens every stored field to float64, its udf.py:18-26).
 """
 
 from __future__ import annotations
+
+from collections.abc import MutableMapping
 
 import numpy as np
 import torch
@@ -19,7 +25,7 @@ __all__ = ["FeatureDict", "NodeBatch", "EdgeBatch"]
 
 
 def take_rows(arr, ids):
-    """arr[ids] for numpy arrays and torch tensors alike."""
+    """``arr[ids]`` for numpy arrays and torch tensors, ids of either kind."""
     if T.is_torch(arr):
         idx = ids if T.is_torch(ids) else torch.from_numpy(np.asarray(ids, dtype=np.int64))
         return arr[idx.to(arr.device)]
@@ -28,132 +34,105 @@ def take_rows(arr, ids):
     return arr[ids]
 
 
-class FeatureDict:
-    """``g.ndata`` / ``g.edata``: field name -> array with one row per node/edge."""
+class FeatureDict(MutableMapping):
+    """Field name -> array whose leading axis has one row per node (``ndata``)
+    or per edge (``edata``).  Assigning an array of another length raises
+    ``ValueError``; reading a missing field raises ``KeyError`` naming it."""
 
     def __init__(self, store: dict, num_rows: int, what: str):
-        self._store = store
-        self._num_rows = num_rows
-        self._what = what
+        # `store` is shared with the graph, which reads fields from it directly
+        self._store, self._num_rows, self._what = store, num_rows, what
+
+    def _noun(self):
+        # "ndata" -> "node", "edata" -> "edge" (the message DGL users know)
+        return {"ndata": "node", "edata": "edge"}.get(self._what, self._what)
 
     def __setitem__(self, key, value):
         arr = T.feature(value)
-        shape = T.shape_of(arr)
-        if len(shape) == 0 or shape[0] != self._num_rows:
+        shape = tuple(T.shape_of(arr))
+        if not shape or shape[0] != self._num_rows:
             raise ValueError("{} expects {} rows, got shape {}".format(
                 self._what, self._num_rows, shape))
         self._store[key] = arr
 
     def __getitem__(self, key):
-        try:
-            return self._store[key]
-        except KeyError:
-            raise KeyError("cannot find {} feature {}".format(self._what[:-1], key))
-
-    def __contains__(self, key):
-        return key in self._store
+        if key not in self._store:
+            raise KeyError("cannot find {} feature {}".format(self._noun(), key))
+        return self._store[key]
 
     def __delitem__(self, key):
         del self._store[key]
 
-    def __len__(self):
-        return len(self._store)
-
     def __iter__(self):
         return iter(self._store)
 
-    def keys(self):
-        return self._store.keys()
+    def __len__(self):
+        return len(self._store)
 
-    def items(self):
-        return self._store.items()
-
-    def pop(self, key, *default):
-        return self._store.pop(key, *default)
+    def __contains__(self, key):
+        return key in self._store
 
     def __repr__(self):
         return repr(self._store)
 
 
-class _EndpointView:
-    """``edges.src`` / ``edges.dst``: node fields gathered at the batch's endpoints."""
+class _Rows:
+    """Read-only field view that gathers the rows ``ids`` of every field it is
+    asked for: ``edges.src`` / ``edges.dst`` over the node store (ids = the
+    batch's endpoints), ``edges.data`` over the edge store (ids = edge ids)."""
 
-    def __init__(self, graph, ids):
-        self._graph = graph
-        self._ids = ids
+    __slots__ = ("_fields", "_ids")
 
-    def __getitem__(self, key):
-        return take_rows(self._graph.ndata[key], self._ids)
-
-    def __contains__(self, key):
-        return key in self._graph.ndata
-
-
-class _EdgeDataView:
-    def __init__(self, graph, eids):
-        self._graph = graph
-        self._eids = eids
+    def __init__(self, fields, ids):
+        self._fields, self._ids = fields, ids
 
     def __getitem__(self, key):
-        return take_rows(self._graph.edata[key], self._eids)
+        return take_rows(self._fields[key], self._ids)
 
     def __contains__(self, key):
-        return key in self._graph.edata
+        return key in self._fields
 
 
 class NodeBatch:
-    """The ``nodes`` argument of a reduce or apply UDF: ``data`` and ``mailbox``."""
+    """What a reduce or apply UDF receives.  ``nodes[f]`` looks in the mailbox
+    first, then in the node data."""
 
     def __init__(self, data=None, mailbox=None, num_nodes: int = 0, batch_num_nodes=None):
-        self._data = data if data is not None else {}
-        self._mailbox = mailbox if mailbox is not None else {}
-        self._num_nodes = num_nodes
+        # the mapping objects are kept, not copied: a UDF sees the live stores
+        self.__fields = ({} if mailbox is None else mailbox, {} if data is None else data)
+        self.__count = int(num_nodes)
+
+    mailbox = property(lambda self: self.__fields[0], doc="messages reduced per node")
+    data = property(lambda self: self.__fields[1], doc="the nodes' own fields")
 
     def __getitem__(self, key):
-        if key in self._mailbox:
-            return self._mailbox[key]
-        return self._data[key]
-
-    @property
-    def mailbox(self):
-        return self._mailbox
-
-    @property
-    def data(self):
-        return self._data
-
-    def batch_num_nodes(self, ntype=None):
-        return [self._num_nodes]
+        for fields in self.__fields:
+            if key in fields:
+                return fields[key]
+        raise KeyError(key)
 
     def num_nodes(self, ntype=None):
-        return self._num_nodes
+        return self.__count
+
+    def batch_num_nodes(self, ntype=None):
+        return [self.__count]
 
     def __repr__(self):
-        return "NodeBatch(num_nodes={}, keys={})".format(
-            self._num_nodes, list(self._mailbox) + list(self._data))
+        keys = [k for fields in self.__fields for k in fields]
+        return "NodeBatch(num_nodes={}, keys={})".format(self.__count, keys)
 
 
 class EdgeBatch:
-    """The ``edges`` argument of a message UDF: ``src``, ``dst`` and ``data``."""
+    """What a message UDF receives: the batch's edges ``eids`` with their
+    source rows (``src``), destination rows (``dst``) and edge rows
+    (``data``)."""
 
     def __init__(self, graph, eids):
-        self._graph = graph
-        self._eids = eids
+        self._graph, self._eids = graph, eids
         u, v = graph._edge_arrays()
-        self._src = _EndpointView(graph, take_rows(u, eids))
-        self._dst = _EndpointView(graph, take_rows(v, eids))
-
-    @property
-    def src(self):
-        return self._src
-
-    @property
-    def dst(self):
-        return self._dst
-
-    @property
-    def data(self):
-        return _EdgeDataView(self._graph, self._eids)
+        self.src = _Rows(graph.ndata, take_rows(u, eids))
+        self.dst = _Rows(graph.ndata, take_rows(v, eids))
+        self.data = _Rows(graph.edata, eids)
 
     @property
     def number_of_nodes(self):

@@ -83,9 +83,9 @@ def test_bf16_tensors(orc):
 
 def test_config4_shape_checksum(orc):
     """BASELINE config 4's shapes at full size (2M x 256 by 64 x 256 x 256):
-    a seeded sample of rows against the oracle, and a size-independent
-    property -- the column sums of out equal sum_r (column sums of a's rows of
-    segment r) @ b[r]."""
+    a seeded sample of rows against the oracle's segment_mm and gather_mm, and
+    a size-independent property -- the column sums of out equal
+    sum_r (column sums of a's rows of segment r) @ b[r]."""
     rng = np.random.default_rng(4)
     n, r, d = 2_000_000, 64, 256
     a = torch.empty((n, d), device="cuda").normal_(0, 0.05, generator=torch.Generator("cuda").manual_seed(4))
@@ -100,10 +100,22 @@ def test_config4_shape_checksum(orc):
             colsum += a[off[i]:off[i + 1]].double().sum(0) @ b[i].double()
     np.testing.assert_allclose(out.double().sum(0).cpu().numpy(), colsum.cpu().numpy(),
                                rtol=2e-2, atol=2e-2 * float(colsum.abs().max()))
-    rows = np.sort(rng.choice(n, 2000, replace=False))
+    # sampled rows, the first and last row of every segment included: the
+    # oracle runs segment_mm on the sampled rows grouped by their relation
+    edges = np.concatenate([off[:-1][seglen > 0], off[1:][seglen > 0] - 1])
+    rows = np.unique(np.concatenate([rng.choice(n, 2000, replace=False), edges]))
     rel = np.searchsorted(off, rows, side="right") - 1
-    a_s = a[torch.from_numpy(rows).cuda()].double().cpu().numpy()
+    rows_t = torch.from_numpy(rows).cuda()
+    a_s = a[rows_t].double().cpu().numpy()
     b_np = b.double().cpu().numpy()
-    ref = np.einsum("ik,ikj->ij", a_s, b_np[rel])
-    s = np.einsum("ik,ikj->ij", np.abs(a_s), np.abs(b_np[rel]))
-    within_s(out[torch.from_numpy(rows).cuda()].double().cpu().numpy(), ref, s)
+    seglen_s = np.bincount(rel, minlength=r)
+    within_s(out[rows_t].double().cpu().numpy(), orc.segment_mm(a_s, b_np, seglen_s),
+             orc.segment_mm(np.abs(a_s), np.abs(b_np), seglen_s))
+    del out
+    # gather_mm at the same size, uniform relation ids (the reference's
+    # segment route at this shape), on the same sample
+    idx = rng.integers(0, r, n)
+    got = ops.gather_mm(a, b, idx_b=torch.from_numpy(idx).cuda())
+    no_device_error()
+    within_s(got[rows_t].double().cpu().numpy(), orc.gather_mm(a_s, b_np, idx[rows]),
+             orc.gather_mm(np.abs(a_s), np.abs(b_np), idx[rows]))
