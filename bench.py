@@ -45,7 +45,6 @@ sys.path.insert(0, ROOT)
 CFG3 = dict(num_nodes=2_500_000, num_edges=125_000_000, dim=128, seed=3)
 METRIC = "gSpMM Gedge-feat/s"
 UNIT = "Gedge-feat/s"
-CPU_SAMPLE_EDGES = 1 << 23
 HALO_SLICES = 4  # feature slices of the multi-GPU halo (one all-gather + one gSpMM pass each)
 
 
@@ -148,48 +147,78 @@ def cpu_threads():
         return os.cpu_count() or 1
 
 
-def cpu_sample(u, v, h, num_nodes, sample_edges):
-    """A dst-row prefix of the graph holding ~sample_edges in-edges, as the
-    reference's in-CSR (stable by destination), for the oracle."""
-    rows = max(1, int(num_nodes * sample_edges / max(u.size, 1)))
-    sel = np.nonzero(v < rows)[0]
-    order = sel[np.argsort(v[sel], kind="stable")]
-    indeg = np.bincount(v[sel], minlength=rows).astype(np.int64)
-    indptr = np.zeros(rows + 1, dtype=np.int64)
-    np.cumsum(indeg, out=indptr[1:])
-    indices = np.ascontiguousarray(u[order], dtype=np.int64)
-    eid = np.arange(order.size, dtype=np.int64)
-    return rows, indptr, indices, eid, indeg
-
-
-def time_oracle(u, v, h, num_nodes, dim, sample_edges, repeats):
-    """The CPU restatement of the reference kernel (fp64, its 32-worker
-    split, every host thread OpenMP offers) on a bounded sample; returns
-    (Gedge-feat/s per repeat, threads, sample description)."""
-    threads = min(32, cpu_threads())
-    # every host thread the reference's 32-worker split can use (torchrun
-    # exports OMP_NUM_THREADS=1 to its ranks; the oracle's OpenMP runtime
-    # reads the variable when it is first loaded, below)
+def oracle_threads(world=1):
+    """Host threads for the oracle: all of them (up to the reference's 32
+    workers) for the timed CPU arm; a share per rank for checks at N > 1.
+    torchrun exports OMP_NUM_THREADS=1 to its ranks and the oracle's OpenMP
+    runtime reads the variable when it is first loaded, so this runs before
+    the first import of oracle."""
+    threads = max(1, min(32, cpu_threads() // max(world, 1)))
     os.environ["OMP_NUM_THREADS"] = str(threads)
+    return threads
+
+
+def host_csr(u, v, num_nodes):
+    """The reference's in-CSR of the whole graph (heterograph.py:69-86) on the
+    host, int64, through the oracle's O(E) counting sort (= stable argsort)."""
+    from oracle import oracle as orc
+
+    indptr, deg, order, indices = orc.csr_arrays(v, u, num_nodes)
+    return indptr, indices, order, deg
+
+
+def time_oracle(csr, h, num_nodes, dim, calls):
+    """The CPU restatement of the reference kernel (fp64, its 32-worker split
+    over every host thread OpenMP offers) on the WHOLE config-3 graph:
+    copy_u_mean through mdgl_gspmm, once per call.  Returns the per-call
+    seconds, the thread count and a description."""
     from oracle import oracle as orc
 
     lib = orc.lib()
-    rows, indptr, indices, eid, indeg = cpu_sample(u, v, h, num_nodes, sample_edges)
+    indptr, indices, eid, deg = csr
     h64 = np.ascontiguousarray(h, dtype=np.float64)  # the reference's f64() gate
-    out = np.empty((rows, dim), dtype=np.float64)
-    ne = int(indices.size)
-    rates = []
-    for _ in range(repeats):
+    out = np.empty((num_nodes, dim), dtype=np.float64)
+    secs = []
+    for _ in range(calls):
         t0 = time.perf_counter()
         lib.mdgl_gspmm(indptr.ctypes.data, indices.ctypes.data, eid.ctypes.data, h64.ctypes.data,
-                       h64.ctypes.data, out.ctypes.data, rows, 5, dim, dim, dim, 3,
-                       indeg.ctypes.data)
-        dt = time.perf_counter() - t0
-        rates.append(ne * dim / dt / 1e9)
-    desc = ("copy_u_mean on the first {} destination rows of config 3 ({} in-edges, "
-            "{:.2%} of the graph), fp64, {} OpenMP threads over the reference's 32-worker "
-            "split".format(rows, ne, ne / max(u.size, 1), int(lib.oref_threads())))
-    return rates, int(lib.oref_threads()), desc
+                       h64.ctypes.data, out.ctypes.data, num_nodes, 5, dim, dim, dim, 3,
+                       deg.ctypes.data)
+        secs.append(time.perf_counter() - t0)
+    desc = ("copy_u_mean over the whole config-3 graph ({} destination rows, {} edges), fp64, "
+            "{} OpenMP threads over the reference's 32-worker split".format(
+                num_nodes, int(indices.size), int(lib.oref_threads())))
+    return secs, int(lib.oref_threads()), desc
+
+
+def check_parity(u, v, h, indeg, out, lo, hi, num_nodes, seed, rows=20_000, top=1000):
+    """Sampled oracle check of a copy_u_mean result: ``out`` holds the rows
+    [lo, hi) (a device tensor or a host array).  ``rows`` random rows of the
+    range plus its ``top`` highest in-degree rows are recomputed by the float64
+    oracle on their own in-edges (oracle/sampled.py) and compared under the
+    suite's float32 bound |got - ref| <= 1e-5 |ref| + 1e-5 S, S = mean |h| of
+    the row's sources.  Runs outside every timed region."""
+    from oracle import oracle as orc
+    from oracle import sampled as smp
+
+    pick = smp.sample_rows(indeg[lo:hi], rows, top, seed) + lo
+    s = smp.RowSample(u, v, pick, num_nodes)
+    local = s.rows - lo
+    if hasattr(out, "cpu"):
+        import torch
+
+        got = out[torch.from_numpy(local).to(out.device)].cpu().numpy()
+    else:
+        got = np.asarray(out)[local]
+    worst, max_err = -np.inf, 0.0
+    for sl, lg in s.batches(1 << 20):
+        hl = h[lg.nodes]
+        ref = orc.gspmm(lg.graph, "copy_lhs", "mean", hl, None)[lg.rows]
+        bound = orc.gspmm(lg.graph, "copy_lhs", "mean", np.abs(hl), None)[lg.rows]
+        ex, me = smp.excess(got[sl], ref, bound, 1e-5)
+        worst, max_err = max(worst, ex), max(max_err, me)
+    return {"rows": int(s.rows.size), "edges": int(s.num_edges), "max_abs_err": max_err,
+            "max_excess": worst, "ok": bool(worst <= 0.0)}
 
 
 # --------------------------------------------------------------- main paths
@@ -199,26 +228,35 @@ def dist_env():
 
 
 def run_reference(args):
+    """The reference's CPU path (the C restatement of its Mojo kernel, which
+    cannot be built here) on the whole config-3 graph: W warm-up calls, then
+    K timed calls; ms_per_step is the best timed call (the reference's own
+    best-of statistic, bench/bench.py:80-86), the median beside it."""
     rank, world, _ = dist_env()
     if rank != 0:
         return 0
+    threads = oracle_threads()
     c = CFG3
+    n, e, d = c["num_nodes"], c["num_edges"], c["dim"]
     u, v, h = make_cfg3(**c)
-    # the warm-up samples are timed like the others and dropped
-    rates, threads, desc = time_oracle(u, v, h, c["num_nodes"], c["dim"], CPU_SAMPLE_EDGES,
-                                       args.warmup + args.steps)
-    rates = rates[args.warmup:]
-    value = statistics.median(rates)
-    ms = c["num_edges"] * c["dim"] / (value * 1e9) * 1e3
+    csr = host_csr(u, v, n)
+    del u, v
+    secs, threads, desc = time_oracle(csr, h, n, d, args.warmup + args.steps)
+    secs = secs[args.warmup:]
+    best, med = min(secs), statistics.median(secs)
+    value = e * d / best / 1e9
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": best * 1e3,
+        "median_ms_per_step": med * 1e3, "statistic": "best of the timed calls",
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
         "data": "synthetic",
-        "config": {"workload": "cfg3 copy_u_mean, N=2.5M, E=125M, D=128 (sampled on CPU)",
-                   "parallelism": "cpu"},
+        "config": {"workload": "cfg3 copy_u_mean (BASELINE config 3): N=2.5M, E=125M "
+                               "lognormal out-degree, D=128, whole graph, fp64 on the host",
+                   "num_nodes": n, "num_edges": e, "dim": d, "seed": c["seed"],
+                   "parallelism": "cpu, {} threads".format(threads)},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": desc},
+                         "sample": desc + " (whole workload, best of {})".format(len(secs))},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference's Mojo library cannot be built in this image (no Mojo toolchain); "
                 "this arm times oracle/ported_ref.c, a C restatement of src/ported.mojo",
@@ -246,6 +284,7 @@ def run_ours(args):
                                    owner_blocks)
 
     rank, world, local = dist_env()
+    oracle_threads(world)  # the parity check (and at N=1 the CPU arm) run the oracle later
     if world > 1:
         torch.cuda.set_device(local)
         import datetime
@@ -314,6 +353,9 @@ def run_ours(args):
     with ClockSampler(local) as clocks:
         ms_step = timed(step, args.steps, args.warmup)
     ms_allgather = timed(step_allgather, args.steps, 1) if world > 1 else None
+    # the all-gather alone (the collective that bounds the step at N > 1)
+    ms_gather_only = (timed(lambda: dist.all_gather_into_tensor(gathered, my_block[:blk]),
+                            args.steps, 1) if world > 1 else None)
     # the gSpMM call alone (coords + main + fixup kernels) for the roofline
     feat = h_dev
     ms_kernel = timed(lambda: shard.copy_u(feat, "mean", out=out, workspace=ws), args.steps, 1)
@@ -330,6 +372,31 @@ def run_ours(args):
                        "achieved_GBps": algorithmic_bytes(hi - lo, shard.shard.num_edges, d,
                                                           arg=arg is not None) / (ms_op * 1e-3) / 1e9}
     del arg_u
+    # the headline op in float64, the reference's precision (same bgl_gspmm)
+    if not args.no_extra:
+        h64 = h_dev.double()
+        out64 = torch.empty((hi - lo, d), dtype=torch.float64, device=dev)
+        ms_op = timed(lambda: shard.copy_u(h64, "mean", out=out64), args.steps, 1)
+        extra["copy_u_mean_f64"] = {
+            "ms": ms_op, "Gedge_feat_s": e_total * d / (ms_op * 1e-3) / 1e9 if world == 1 else None,
+            "achieved_GBps": algorithmic_bytes(hi - lo, shard.shard.num_edges, d, elem=8)
+            / (ms_op * 1e-3) / 1e9}
+        del h64, out64
+
+    # -------- parity: the timed step's result rows, sampled, against the
+    # oracle (after every timed region; each rank checks its own rows)
+    step()
+    torch.cuda.synchronize()
+    parity = check_parity(u, v, h, indeg, out, lo, hi, n, seed=300 + rank)
+    if world > 1:
+        t = torch.tensor([parity["max_excess"], parity["max_abs_err"], parity["rows"],
+                          parity["edges"]], dtype=torch.float64, device=dev)
+        w = t.clone()
+        dist.all_reduce(w, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        parity = {"rows": int(t[2]), "edges": int(t[3]), "max_abs_err": float(w[1]),
+                  "max_excess": float(w[0]), "ok": bool(float(w[0]) <= 0.0),
+                  "ranks": world}
 
     # -------- e2e through the public API with host buffers
     e2e = None
@@ -353,7 +420,9 @@ def run_ours(args):
         dt = (time.perf_counter() - t0) / args.steps
         e2e = {"value": e_total * d / dt / 1e9, "unit": UNIT,
                "h2d_bytes_per_step": int(h.nbytes), "d2h_bytes_per_step": int(r.numel() * 4),
-               "ms_per_step": dt * 1e3, "path": "ops.copy_u_mean(g, pinned CPU tensor)"}
+               "ms_per_step": dt * 1e3, "path": "ops.copy_u_mean(g, pinned CPU tensor)",
+               "parity": check_parity(u, v, h, indeg, r.numpy(), 0, n, n, seed=400,
+                                      rows=5000, top=100)}
         del g, h_pin, r
     else:
         h_pin = torch.from_numpy(np.ascontiguousarray(h[own_lo:own_hi])).pin_memory()
@@ -406,9 +475,12 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        rates, threads, desc = time_oracle(u, v, h, n, d, CPU_SAMPLE_EDGES, 3)
-        cpu = {"value": max(rates), "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": desc + " (best of 3)"}
+        csr = host_csr(u, v, n)
+        secs, threads, desc = time_oracle(csr, h, n, d, 3)
+        del csr
+        cpu = {"value": e_total * d / min(secs) / 1e9, "unit": UNIT, "cores": threads,
+               "kind": "port", "ms": min(secs) * 1e3,
+               "sample": desc + " (whole workload, best of 3)"}
 
     if rank == 0:
         line = {
@@ -427,11 +499,15 @@ def run_ours(args):
             # per gSpMM call: coordinates, main and fixup kernels; at N > 1 one
             # call per halo slice (the all-gathers are NCCL's kernels)
             "gpu_launches": 3 * (HALO_SLICES if world > 1 else 1) * args.steps,
-            "clocks": clocks.summary(), "ops": extra,
+            "clocks": clocks.summary(), "ops": extra, "parity": parity,
             "allgather_then_compute": None if ms_allgather is None else
             {"value": e_total * d / (ms_allgather * 1e-3) / 1e9, "unit": UNIT,
              "ms_per_step": ms_allgather,
              "what": "one NCCL all-gather of the features, then the local gSpMM (no overlap)"},
+            "allgather_only": None if ms_gather_only is None else
+            {"ms": ms_gather_only, "bytes_received_per_rank": blk * (world - 1) * d * 4,
+             "GBps_per_rank": blk * (world - 1) * d * 4 / (ms_gather_only * 1e-3) / 1e9,
+             "what": "one NCCL all_gather_into_tensor of the owner blocks (the step's halo), alone"},
             "compute_only": {"value": e_total * d / (ms_kernel * 1e-3) / 1e9, "unit": UNIT,
                              "ms_per_step": ms_kernel,
                              "what": "local gSpMM only (features already replicated), max over ranks"},
@@ -574,7 +650,7 @@ def run_suite(args):
         torch.cuda.empty_cache()
     if "cfg4" in want:
         rng = np.random.default_rng(4)
-        n, r, d = 2_000_000, 64, 256
+        n, r, d = int(2_000_000 * sc), 64, 256
         gen.manual_seed(4)
         a = torch.empty((n, d), device="cuda").normal_(0, 0.05, generator=gen)
         b = torch.empty((r, d, d), device="cuda").normal_(0, 0.05, generator=gen)
@@ -627,7 +703,8 @@ def main():
     ap.add_argument("--suite", default="",
                     help="time every op of the named configs (cfg2,cfg3,cfg4,cfg5 or all) instead")
     ap.add_argument("--suite-scale", type=float, default=1.0,
-                    help="scale configs 2 and 5 (nodes and edges) in --suite (profiling cases)")
+                    help="scale configs 2 and 5 (nodes and edges) and config 4 (rows) in --suite "
+                         "(profiling cases)")
     ap.add_argument("--scale", type=float, default=1.0,
                     help="scale the edge count (a smaller case for profiling; nodes unchanged)")
     args = ap.parse_args()

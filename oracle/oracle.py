@@ -43,7 +43,7 @@ _SIGS = {
     "mdgl_cumsum": 3, "mdgl_replace_inf_with_zero": 3, "mdgl_clamp_i64": 5,
     "mdgl_gsddmm": 12, "mdgl_gspmm": 13, "mdgl_segment_reduce": 7,
     "mdgl_segment_softmax": 7, "mdgl_segment_mm": 8, "mdgl_edge_softmax_": 10,
-    "mdgl_gather_mm": 7, "oref_gspmm_arg": 15,
+    "mdgl_gather_mm": 7, "oref_gspmm_arg": 15, "oref_csr_build": 8,
 }
 _lib = None
 
@@ -122,6 +122,20 @@ class Graph:
 
     def out_csr(self):
         return self.outptr, self.out_indices, self.out_order
+
+
+def csr_arrays(key, other, num_nodes):
+    """(indptr, deg, order, indices) of the CSR keyed by ``key``
+    (heterograph.py:69-86) through the C counting sort: identical to the
+    stable-argsort construction of Graph, in O(E) for full-size graphs."""
+    key, other = i64(key), i64(other)
+    n, e = int(num_nodes), int(key.size)
+    indptr = np.empty(n + 1, dtype=np.int64)
+    deg = np.empty(n, dtype=np.int64)
+    order = np.empty(e, dtype=np.int64)
+    indices = np.empty(e, dtype=np.int64)
+    lib().oref_csr_build(_a(key), _a(other), e, n, _a(indptr), _a(deg), _a(order), _a(indices))
+    return indptr, deg, order, indices
 
 
 # ------------------------------------------------------ shape handling (sddmm)

@@ -32,6 +32,7 @@
  */
 #include <math.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #ifdef _OPENMP
@@ -397,4 +398,27 @@ i64 oref_threads(void) {
 #else
     return 1;
 #endif
+}
+
+/* The reference's in-CSR build (python/mojodgl/heterograph.py:69-86):
+ * deg = bincount(key), indptr = [0, cumsum(deg)], order = argsort(key,
+ * kind="stable"), indices = other[order].  A counting sort is a stable
+ * argsort of integer keys, so this is the same arrays in O(E) (the timed CPU
+ * arm builds config 3's 125M-edge CSR with it; it is not timed itself). */
+void oref_csr_build(i64 key_, i64 other_, i64 num_edges, i64 num_nodes, i64 indptr_, i64 deg_,
+                    i64 order_, i64 indices_) {
+    const i64 *key = IP(key_), *other = IP(other_);
+    i64 *indptr = IP(indptr_), *deg = IP(deg_), *order = IP(order_), *indices = IP(indices_);
+    memset(deg, 0, (size_t)num_nodes * sizeof(i64));
+    for (i64 e = 0; e < num_edges; ++e) deg[key[e]] += 1;
+    indptr[0] = 0;
+    for (i64 v = 0; v < num_nodes; ++v) indptr[v + 1] = indptr[v] + deg[v];
+    i64 *next = (i64 *)malloc((size_t)(num_nodes > 0 ? num_nodes : 1) * sizeof(i64));
+    memcpy(next, indptr, (size_t)num_nodes * sizeof(i64));
+    for (i64 e = 0; e < num_edges; ++e) {
+        i64 p = next[key[e]]++;
+        order[p] = e;
+        indices[p] = other[e];
+    }
+    free(next);
 }
