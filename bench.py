@@ -10,19 +10,27 @@ numpy.random.default_rng(3).  One step = one gSpMM copy_u_mean over all edges
 (``ops.copy_u_mean``), the config's first op; copy_u_max with arg-index output
 and copy_u_sum are timed beside it under "ops".
 
-Multi-GPU (torchrun, one rank per GPU): strong scaling of the same graph,
-destination rows partitioned by in-edge count, features owned in equal row
-blocks.  A step gathers the feature blocks slice by slice (each owner block
-cut into HALO_SLICES row slices, one NCCL all-gather per slice) and runs one
-accumulating gSpMM pass over the rank's edges whose sources fall in a slice as
-soon as it is in, while the next slice is gathered, so the halo overlaps the
-aggregation;
-"allgather_then_compute" times the unpipelined alternative (one all-gather,
-then the local gSpMM) and "compute_only" the local gSpMM alone.
+Multi-GPU (torchrun, one rank per GPU): strong scaling of the same graph on
+an R x C rank grid (C = --cols, by default GRID_COLS[N]): a rank aggregates
+the destination rows of its row group (R ranges balanced by in-edge count)
+for the feature columns of its column group (C contiguous column blocks), and
+owns one block of rows of its column block.  A step gathers the column
+group's owner blocks slice by slice (each block cut into --halo-slices row
+slices, one NCCL all-gather per slice within the column group) and runs one
+accumulating gSpMM pass over the rank's edges whose sources fall in a slice
+as soon as it is in, while the next slice is gathered, so the halo overlaps
+the aggregation; with one row group (R = 1) a rank already holds every row of
+its columns and the step is one gSpMM.  "allgather_then_compute" times the
+unpipelined alternative (one all-gather, then the local gSpMM),
+"allgather_only" the collective alone and "compute_only" the local gSpMM
+alone.
+
+After every timed region the step's result is checked on a seeded sample of
+rows against the float64 oracle ("parity"; each rank its own rows).
 
 Prints one JSON line (rank 0).  ``--impl reference`` times the CPU
 restatement of the reference's Mojo kernels (oracle/, the reference itself
-cannot be built here) on the same workload and prints its line.
+cannot be built here) on the whole config-3 workload and prints its line.
 """
 
 from __future__ import annotations
@@ -46,6 +54,8 @@ CFG3 = dict(num_nodes=2_500_000, num_edges=125_000_000, dim=128, seed=3)
 METRIC = "gSpMM Gedge-feat/s"
 UNIT = "Gedge-feat/s"
 HALO_SLICES = 4  # feature slices of the multi-GPU halo (one all-gather + one gSpMM pass each)
+# column groups of the rank grid by GPU count (R = N / C row groups)
+GRID_COLS = {2: 2, 4: 2, 8: 2}
 
 
 # ----------------------------------------------------------------- workload
@@ -280,8 +290,8 @@ def run_ours(args):
 
     import mojodgl as dgl
     from mojodgl import ops
-    from mojodgl.partition import (DeviceShard, DstShard, SlicePipeline, edge_balanced_ranges,
-                                   owner_blocks)
+    from mojodgl.partition import (DeviceShard, DstShard, SlicePipeline, column_group_ranks,
+                                   column_range, edge_balanced_ranges, owner_blocks, rank_grid)
 
     rank, world, local = dist_env()
     oracle_threads(world)  # the parity check (and at N=1 the CPU arm) run the oracle later
@@ -297,37 +307,53 @@ def run_ours(args):
     n, e_total, d = c["num_nodes"], c["num_edges"], c["dim"]
     u, v, h = make_cfg3(**c)
 
-    # -------- graph shard on this rank: dst rows balanced by in-edges
+    # -------- this rank's place in the R x C grid, its graph shard (dst rows
+    # balanced by in-edges within its row group) and its feature columns
+    cols = args.cols if args.cols > 0 else GRID_COLS.get(world, 1)
+    rows_n, rg, cg = rank_grid(rank, world, cols)
+    grp = None
+    if world > 1 and cols > 1:
+        # every rank creates every column group, in the same order
+        groups = [dist.new_group(r) for r in column_group_ranks(world, cols)]
+        grp = groups[cg]
     indeg = np.bincount(v, minlength=n)
-    bounds = edge_balanced_ranges(indeg, world)
-    lo, hi = int(bounds[rank]), int(bounds[rank + 1])
+    bounds = edge_balanced_ranges(indeg, rows_n)
+    lo, hi = int(bounds[rg]), int(bounds[rg + 1])
+    c0, c1 = column_range(d, cols, cg)
+    dc = c1 - c0
     shard = DeviceShard(DstShard(u, v, lo, hi))
-    pipe = SlicePipeline(u, v, lo, hi, rank, world, n, slices=HALO_SLICES) if world > 1 else None
-    blk, owners = owner_blocks(n, world)
-    own_lo, own_hi = owners[rank]
-    h_dev = torch.from_numpy(h).to(dev)  # full features (kernel-only timing)
-    gathered = torch.empty((blk * world, d), dtype=torch.float32, device=dev)
+    pipe = (SlicePipeline(u, v, lo, hi, rg, rows_n, n, slices=args.halo_slices, group=grp)
+            if rows_n > 1 else None)
+    blk, owners = owner_blocks(n, rows_n)
+    own_lo, own_hi = owners[rg]
+    hc = np.ascontiguousarray(h[:, c0:c1]) if cols > 1 else h
+    # this rank's feature columns for every row: with one row group that is
+    # the rank's own data; otherwise it serves the kernel-only timings
+    h_dev = torch.from_numpy(hc).to(dev)
+    gathered = torch.empty((blk * rows_n, dc), dtype=torch.float32, device=dev)
     # this rank's owner block, padded to whole slices for the sliced gather
-    my_block = torch.zeros((pipe.block_rows() if pipe else blk, d), dtype=torch.float32, device=dev)
+    my_block = torch.zeros((pipe.block_rows() if pipe else blk, dc), dtype=torch.float32,
+                           device=dev)
     my_block[: own_hi - own_lo] = h_dev[own_lo:own_hi]
-    out = torch.empty((hi - lo, d), dtype=torch.float32, device=dev)
+    out = torch.empty((hi - lo, dc), dtype=torch.float32, device=dev)
     ws = None
     torch.cuda.synchronize()
 
-    bufs = ([torch.empty((world * pipe.sb, d), dtype=torch.float32, device=dev) for _ in range(2)]
-            if world > 1 else None)
+    bufs = ([torch.empty((rows_n * pipe.sb, dc), dtype=torch.float32, device=dev)
+             for _ in range(2)] if pipe else None)
     pws = [None]
 
     def step():
-        # the halo overlapped with the aggregation: one pass per owner block
-        # as the blocks come in over a ring of NCCL send/recv
-        if world > 1:
+        # the halo overlapped with the aggregation: slice c of every owner
+        # block of the column group arrives by one all-gather while the pass
+        # over slice c - 1 runs; one row group needs no exchange
+        if pipe:
             pipe.copy_u(my_block, "mean", out, bufs=bufs, ws=pws)
         else:
             shard.copy_u(h_dev, "mean", out=out, workspace=ws)
 
     def step_allgather():
-        dist.all_gather_into_tensor(gathered, my_block[:blk])
+        dist.all_gather_into_tensor(gathered, my_block[:blk], group=grp)
         shard.copy_u(gathered, "mean", out=out, workspace=ws)
 
     def timed(fn, steps, warmup):
@@ -352,10 +378,11 @@ def run_ours(args):
     # the whole step (halo + local gSpMM): the headline value
     with ClockSampler(local) as clocks:
         ms_step = timed(step, args.steps, args.warmup)
-    ms_allgather = timed(step_allgather, args.steps, 1) if world > 1 else None
-    # the all-gather alone (the collective that bounds the step at N > 1)
-    ms_gather_only = (timed(lambda: dist.all_gather_into_tensor(gathered, my_block[:blk]),
-                            args.steps, 1) if world > 1 else None)
+    ms_allgather = timed(step_allgather, args.steps, 1) if pipe else None
+    # the all-gather alone (the collective that bounds the step when R > 1)
+    ms_gather_only = (timed(lambda: dist.all_gather_into_tensor(gathered, my_block[:blk],
+                                                                group=grp),
+                            args.steps, 1) if pipe else None)
     # the gSpMM call alone (coords + main + fixup kernels) for the roofline
     feat = h_dev
     ms_kernel = timed(lambda: shard.copy_u(feat, "mean", out=out, workspace=ws), args.steps, 1)
@@ -363,23 +390,23 @@ def run_ours(args):
 
     # other ops of the config, device resident, this rank's shard
     extra = {}
-    arg_u = torch.empty((hi - lo, d), dtype=torch.int64, device=dev)
+    arg_u = torch.empty((hi - lo, dc), dtype=torch.int64, device=dev)
     for name, red, arg in (() if args.no_extra else
                            (("copy_u_sum", "sum", None), ("copy_u_max+arg_u", "max", arg_u))):
         ms_op = timed(lambda: shard.copy_u(feat, red, out=out, arg_u=arg), args.steps, 1)
         extra[name] = {"ms": ms_op, "Gedge_feat_s": e_total * d / (ms_op * 1e-3) / 1e9 if world == 1
                        else None,
-                       "achieved_GBps": algorithmic_bytes(hi - lo, shard.shard.num_edges, d,
+                       "achieved_GBps": algorithmic_bytes(hi - lo, shard.shard.num_edges, dc,
                                                           arg=arg is not None) / (ms_op * 1e-3) / 1e9}
     del arg_u
     # the headline op in float64, the reference's precision (same bgl_gspmm)
     if not args.no_extra:
         h64 = h_dev.double()
-        out64 = torch.empty((hi - lo, d), dtype=torch.float64, device=dev)
+        out64 = torch.empty((hi - lo, dc), dtype=torch.float64, device=dev)
         ms_op = timed(lambda: shard.copy_u(h64, "mean", out=out64), args.steps, 1)
         extra["copy_u_mean_f64"] = {
             "ms": ms_op, "Gedge_feat_s": e_total * d / (ms_op * 1e-3) / 1e9 if world == 1 else None,
-            "achieved_GBps": algorithmic_bytes(hi - lo, shard.shard.num_edges, d, elem=8)
+            "achieved_GBps": algorithmic_bytes(hi - lo, shard.shard.num_edges, dc, elem=8)
             / (ms_op * 1e-3) / 1e9}
         del h64, out64
 
@@ -387,7 +414,7 @@ def run_ours(args):
     # oracle (after every timed region; each rank checks its own rows)
     step()
     torch.cuda.synchronize()
-    parity = check_parity(u, v, h, indeg, out, lo, hi, n, seed=300 + rank)
+    parity = check_parity(u, v, hc, indeg, out, lo, hi, n, seed=300 + rank)
     if world > 1:
         t = torch.tensor([parity["max_excess"], parity["max_abs_err"], parity["rows"],
                           parity["edges"]], dtype=torch.float64, device=dev)
@@ -425,12 +452,16 @@ def run_ours(args):
                                       rows=5000, top=100)}
         del g, h_pin, r
     else:
-        h_pin = torch.from_numpy(np.ascontiguousarray(h[own_lo:own_hi])).pin_memory()
-        out_pin = torch.empty((hi - lo, d), dtype=torch.float32).pin_memory()
+        # per rank: its owned piece of h (host, pinned) in, its output piece out
+        h_pin = torch.from_numpy(np.ascontiguousarray(hc[own_lo:own_hi] if pipe else hc)).pin_memory()
+        out_pin = torch.empty((hi - lo, dc), dtype=torch.float32).pin_memory()
 
         def e2e_step():
-            my_block[: own_hi - own_lo].copy_(h_pin, non_blocking=True)
-            pipe.copy_u(my_block, "mean", out, bufs=bufs, ws=pws)
+            if pipe:
+                my_block[: own_hi - own_lo].copy_(h_pin, non_blocking=True)
+            else:
+                h_dev.copy_(h_pin, non_blocking=True)
+            step()
             out_pin.copy_(out, non_blocking=True)
             torch.cuda.current_stream().synchronize()
 
@@ -447,8 +478,9 @@ def run_ours(args):
         e2e = {"value": e_total * d / dt / 1e9, "unit": UNIT,
                "h2d_bytes_per_step": int(h.nbytes), "d2h_bytes_per_step": int(n * d * 4),
                "ms_per_step": dt * 1e3,
-               "path": "per rank: pinned h block H2D, sliced all-gather halo overlapped with gSpMM passes, "
-                       "output rows D2H"}
+               "path": "per rank: its pinned piece of h H2D, sliced all-gather halo within its "
+                       "column group overlapped with gSpMM passes (none with one row group), its "
+                       "output piece D2H"}
 
     # -------- roofline of the dominant kernel (this rank's gSpMM)
     peaks = {}
@@ -458,9 +490,9 @@ def run_ours(args):
     except (OSError, ValueError):
         pass
     peak = float(peaks.get("hbm_gbs", 6650.0))
-    alg = algorithmic_bytes(hi - lo, shard.shard.num_edges, d)
+    alg = algorithmic_bytes(hi - lo, shard.shard.num_edges, dc)
     achieved = alg / (ms_kernel * 1e-3) / 1e9
-    traffic = load_traffic().get("cfg3_copy_u_mean_world{}".format(world))
+    traffic = load_traffic().get("cfg3_copy_u_mean_world{}".format(world)) if cols == 1 else None
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "traffic": traffic,
                 "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
@@ -492,21 +524,27 @@ def run_ours(args):
                                    "cfg3 copy_u_mean with edges scaled by {} (profiling case)"
                                    .format(args.scale),
                        "num_nodes": n, "num_edges": e_total, "dim": d, "seed": c["seed"],
-                       "parallelism": "dst-row shards x{} + sliced all-gather halo overlapped with gSpMM passes".format(world)
-                       if world > 1 else "single GPU",
+                       "parallelism": "single GPU" if world == 1 else
+                       "{} x {} rank grid: dst-row shards x{} (balanced by in-edges) x feature-column "
+                       "blocks x{}; {}".format(rows_n, cols, rows_n, cols,
+                                               "halo by {} sliced all-gathers per step within each "
+                                               "column group, overlapped with gSpMM passes".format(
+                                                   args.halo_slices) if pipe else
+                                               "no exchange (each rank owns its column block)"),
+                       "grid": [rows_n, cols], "halo_slices": args.halo_slices if pipe else 0,
                        "l2": "inputs larger than L2 (h 1.28 GB, indices 0.5 GB)"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
             # per gSpMM call: coordinates, main and fixup kernels; at N > 1 one
             # call per halo slice (the all-gathers are NCCL's kernels)
-            "gpu_launches": 3 * (HALO_SLICES if world > 1 else 1) * args.steps,
+            "gpu_launches": 3 * (args.halo_slices if pipe else 1) * args.steps,
             "clocks": clocks.summary(), "ops": extra, "parity": parity,
             "allgather_then_compute": None if ms_allgather is None else
             {"value": e_total * d / (ms_allgather * 1e-3) / 1e9, "unit": UNIT,
              "ms_per_step": ms_allgather,
              "what": "one NCCL all-gather of the features, then the local gSpMM (no overlap)"},
             "allgather_only": None if ms_gather_only is None else
-            {"ms": ms_gather_only, "bytes_received_per_rank": blk * (world - 1) * d * 4,
-             "GBps_per_rank": blk * (world - 1) * d * 4 / (ms_gather_only * 1e-3) / 1e9,
+            {"ms": ms_gather_only, "bytes_received_per_rank": blk * (rows_n - 1) * dc * 4,
+             "GBps_per_rank": blk * (rows_n - 1) * dc * 4 / (ms_gather_only * 1e-3) / 1e9,
              "what": "one NCCL all_gather_into_tensor of the owner blocks (the step's halo), alone"},
             "compute_only": {"value": e_total * d / (ms_kernel * 1e-3) / 1e9, "unit": UNIT,
                              "ms_per_step": ms_kernel,
@@ -700,6 +738,10 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     ap.add_argument("--no-extra", action="store_true", help="skip the other ops of the config")
+    ap.add_argument("--cols", type=int, default=0,
+                    help="column groups of the N>1 rank grid (0: the default for N)")
+    ap.add_argument("--halo-slices", type=int, default=HALO_SLICES,
+                    help="row slices of each owner block in the N>1 halo")
     ap.add_argument("--suite", default="",
                     help="time every op of the named configs (cfg2,cfg3,cfg4,cfg5 or all) instead")
     ap.add_argument("--suite-scale", type=float, default=1.0,

@@ -183,7 +183,6 @@ GmmLayout gmm_layout(void *ws, int64_t n, int64_t d1, int64_t r, int64_t d2, int
     const bool tc = gmm_tensor_core_supported(d1, d2, dtype);
     const size_t elem = dtype == BGL_BF16 ? 2 : 4;
     l.tc_b = tc ? c.take<char>(size_t(r) * d1 * d2 * elem) : nullptr;
-    l.tc_a = (tc && gather) ? c.take<char>(size_t(n) * d1 * elem) : nullptr;
     l.sort_temp_bytes = gather ? sort_bytes(n, r) : 0;
     l.sort_temp = gather ? c.take<char>(l.sort_temp_bytes) : nullptr;
     l.bytes = c.used + 256;

@@ -18,7 +18,6 @@ struct GmmLayout {
     int32_t *iota;
     int32_t *perm;
     void *tc_b;  // tensor-core path: K-major copy of B (r x d2 x d1)
-    void *tc_a;  // tensor-core gather_mm: A's rows grouped by relation
     void *sort_temp;
     size_t sort_temp_bytes;
     int64_t tile_rows;

@@ -2,21 +2,26 @@
 // src/ported.mojo:773-804 and the per-row src/ported.mojo:1089-1130).
 //
 // A persistent, warp-specialised kernel, one CTA per SM walking 128-row x
-// BN-column tiles (a tile never crosses a segment).  Warp 0 streams A rows and
-// the segment's K-major B block by TMA in 128-byte K slices (32 fp32 or 64
-// bf16 values, SWIZZLE_128B) through a ring of kStages stages; warp 1 (one
-// elected thread) issues tcgen05.mma (kind::tf32 for fp32 inputs, kind::f16
-// with bf16 for bf16 inputs) into one of two 128 x BN fp32 accumulators in
-// tensor memory; warps 2-5 read the other accumulator back with tcgen05.ld
-// (each warp its 32-lane quarter), transpose them through shared memory and
-// store whole row segments (rows scattered through `perm` for gather_mm)
-// while the next tile's loads and MMAs run.
+// BN-column tiles (a tile never crosses a segment).  A rows and the segment's
+// K-major B block arrive in 128-byte K slices (32 fp32 or 64 bf16 values,
+// SWIZZLE_128B layout) through two rings of their own: kStagesA slices of A
+// (a DRAM stream, so the deeper ring) and kStagesB slices of B (a block that
+// stays in L2).  Warp 0 issues B's TMA loads; warp 6 issues A's (segment_mm),
+// or, for gather_mm, warps 6-9 gather each tile's A rows through the row
+// permutation with 16-byte cp.async copies straight into the swizzled stage
+// (no materialised copy of the gathered rows).  Warp 1 (one elected thread)
+// issues tcgen05.mma (kind::tf32 for fp32 inputs, kind::f16 with bf16 for bf16
+// inputs) into one of two 128 x BN fp32 accumulators in tensor memory; warps
+// 2-5 read the other accumulator back with tcgen05.ld (each warp its 32-lane
+// quarter), transpose them through shared memory and store whole row segments
+// (rows scattered through `perm` for gather_mm) while the next tile's loads and
+// MMAs run.
 //
 // Every mbarrier wait is bounded (kTimeoutNs of %globaltimer); the first to
 // expire records an error code in g_bgl_tc_error and raises a CTA-wide abort
-// flag that ends every role's loop; the producer then waits (bounded) for the
-// loads it issued and the MMA thread for the MMAs it issued, so no copy or MMA
-// is in flight when the tensor memory is freed and the CTA exits.
+// flag that ends every role's loop; the producers then wait (bounded) for the
+// loads they issued and the MMA thread for the MMAs it issued, so no copy or
+// MMA is in flight when the tensor memory is freed and the CTA exits.
 #include <cuda.h>
 #include <cuda_bf16.h>
 
@@ -31,10 +36,16 @@ __device__ int g_bgl_tc_error = 0;
 namespace {
 
 constexpr int kBM = 128;
-constexpr int kStages = 4;
-constexpr int kThreads = 192;  // producer warp, MMA warp, 4 epilogue warps
+constexpr int kStagesA = 6;  // A slices in flight (DRAM latency)
+constexpr int kStagesB = 3;  // B slices in flight (L2 latency)
+constexpr int kGatherLag = kStagesA - 2;  // cp.async groups a gather thread keeps open
 constexpr int kStageRowBytes = 128;  // epilogue staging: 32 fp32 (or bf16 pairs) per row
+constexpr int kABytes = kBM * 128;   // one A slice: 128 rows x 128 bytes
 constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
+
+// Warp roles.
+constexpr int kWarpB = 0, kWarpMma = 1, kWarpEpi0 = 2, kWarpA0 = 6;
+__host__ __device__ constexpr int threads_for(bool gather) { return 32 * (kWarpA0 + (gather ? 4 : 1)); }
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -99,6 +110,26 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
         : "memory");
 }
 
+// 16-byte cp.async into shared memory; src_bytes = 0 writes zeros (a row past
+// the segment, or K past d1) without reading.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+                 "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// Makes this thread's completed generic-proxy shared-memory writes (cp.async)
+// visible to the async proxy that tcgen05.mma reads its operands through.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // K-major, SWIZZLE_128B shared-memory matrix descriptor: rows of 128 bytes,
 // 8-row groups 1024 bytes apart (SBO), LBO unused (1), version 1, layout 2.
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
@@ -148,6 +179,8 @@ __device__ __forceinline__ void tmem_wait_ld() {
 
 struct TcArgs {
     void *out;
+    const void *a;        // gather_mm: the A rows, read through perm
+    int64_t a_row_bytes;  // gather_mm: bytes of one A row (d1 * element size)
     const int64_t *seg_off;
     const int64_t *tile_off;
     const int32_t *perm;  // gather_mm: output row of permuted row i
@@ -180,33 +213,40 @@ __device__ __forceinline__ void tile_rows(const TcArgs &args, int64_t tile, int6
     row_end = args.seg_off[rel + 1];
 }
 
-template <bool BF16>
-__global__ void __launch_bounds__(kThreads, 1)
+template <bool BF16, bool GATHER>
+__global__ void __launch_bounds__(threads_for(GATHER), 1)
     k_gmm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
              const TcArgs args) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t row_tiles = args.tile_off[args.r];
     const int64_t work = row_tiles * args.nbn;  // (row tile, column tile) pairs
-    const uint32_t a_bytes = kBM * 128, b_bytes = (uint32_t)args.bn * 128;
+    const uint32_t b_bytes = (uint32_t)args.bn * 128;
     // stage buffers, each 1024-byte aligned (the SWIZZLE_128B atom)
     uintptr_t base = (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023);
     unsigned char *sa = reinterpret_cast<unsigned char *>(base);
-    unsigned char *sb = sa + kStages * a_bytes;
+    unsigned char *sb = sa + kStagesA * kABytes;
     // epilogue staging: per epilogue warp 32 rows x 128 bytes
-    uint4 *staging = reinterpret_cast<uint4 *>(sb + kStages * b_bytes);
-    uint64_t *full = reinterpret_cast<uint64_t *>(sb + kStages * b_bytes + 4 * kStageRowBytes * 32);
-    uint64_t *empty = full + kStages;
-    uint64_t *acc_full = empty + kStages;  // [2]: accumulator b holds a finished tile
-    uint64_t *acc_empty = acc_full + 2;    // [2]: the epilogue has read accumulator b
+    uint4 *staging = reinterpret_cast<uint4 *>(sb + kStagesB * b_bytes);
+    uint64_t *a_full = reinterpret_cast<uint64_t *>(sb + kStagesB * b_bytes + 4 * kStageRowBytes * 32);
+    uint64_t *a_empty = a_full + kStagesA;
+    uint64_t *b_full = a_empty + kStagesA;
+    uint64_t *b_empty = b_full + kStagesB;
+    uint64_t *acc_full = b_empty + kStagesB;  // [2]: accumulator b holds a finished tile
+    uint64_t *acc_empty = acc_full + 2;       // [2]: the epilogue has read accumulator b
     uint64_t *mma_done = acc_empty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
+        for (int s = 0; s < kStagesA; ++s) {
+            // gather: one arrive per gather thread once its copies have landed
+            mbar_init(&a_full[s], GATHER ? 128 : 1);
+            mbar_init(&a_empty[s], 1);
+        }
+        for (int s = 0; s < kStagesB; ++s) {
+            mbar_init(&b_full[s], 1);
+            mbar_init(&b_empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&acc_full[b], 1);
@@ -217,7 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     const uint32_t acc_cols = args.bn <= 32 ? 32 : args.bn <= 64 ? 64 : args.bn <= 128 ? 128 : 256;
-    if (warp == 1) {
+    if (warp == kWarpMma) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(tmem_slot)),
                      "r"(2 * acc_cols));
@@ -229,9 +269,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = *tmem_slot;
     const int kb_n = args.kb;
 
-    if (warp == 0) {
+    if (warp == kWarpB) {
         if (lane == 0) {
-            // TMA producer: k-iteration `it` counts across this CTA's tiles
+            // B producer: slice `it` counts across this CTA's tiles
             int64_t it = 0;
             bool ok = true;
             for (int64_t w = blockIdx.x; w < work && ok; w += gridDim.x) {
@@ -239,22 +279,93 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tile_rows(args, w / args.nbn, rel, row0, row_end);
                 const int32_t nb = (int32_t)(w % args.nbn);
                 for (int kb = 0; kb < kb_n; ++kb, ++it) {
-                    const int s = (int)(it % kStages);
-                    if (it >= kStages &&
-                        !(ok = mbar_wait(&empty[s], (uint32_t)((it / kStages) - 1) & 1, 1, abort)))
+                    const int s = (int)(it % kStagesB);
+                    if (it >= kStagesB &&
+                        !(ok = mbar_wait(&b_empty[s], (uint32_t)((it / kStagesB) - 1) & 1, 1, abort)))
                         break;
-                    mbar_arrive_expect_tx(&full[s], a_bytes + b_bytes);
-                    const int32_t kx = kb * (BF16 ? 64 : 32);
-                    tma_load_2d(sa + s * a_bytes, &map_a, &full[s], kx, (int32_t)row0);
-                    tma_load_2d(sb + s * b_bytes, &map_b, &full[s], kx,
+                    mbar_arrive_expect_tx(&b_full[s], b_bytes);
+                    tma_load_2d(sb + s * b_bytes, &map_b, &b_full[s], kb * (BF16 ? 64 : 32),
                                 (int32_t)(rel * args.d2 + (int64_t)nb * args.bn));
                 }
             }
             // the last issued loads (at most one per stage) have landed before exit
-            for (int64_t j = (it > kStages ? it - kStages : 0); j < it; ++j)
-                mbar_wait(&full[j % kStages], (uint32_t)(j / kStages) & 1, 2, nullptr);
+            for (int64_t j = (it > kStagesB ? it - kStagesB : 0); j < it; ++j)
+                mbar_wait(&b_full[j % kStagesB], (uint32_t)(j / kStagesB) & 1, 2, nullptr);
         }
-    } else if (warp == 1) {
+    } else if (!GATHER && warp == kWarpA0) {
+        if (lane == 0) {
+            // A producer (segment_mm): TMA tile loads of 128 rows
+            int64_t it = 0;
+            bool ok = true;
+            for (int64_t w = blockIdx.x; w < work && ok; w += gridDim.x) {
+                int64_t rel, row0, row_end;
+                tile_rows(args, w / args.nbn, rel, row0, row_end);
+                for (int kb = 0; kb < kb_n; ++kb, ++it) {
+                    const int s = (int)(it % kStagesA);
+                    if (it >= kStagesA &&
+                        !(ok = mbar_wait(&a_empty[s], (uint32_t)((it / kStagesA) - 1) & 1, 1, abort)))
+                        break;
+                    mbar_arrive_expect_tx(&a_full[s], kABytes);
+                    tma_load_2d(sa + s * kABytes, &map_a, &a_full[s], kb * (BF16 ? 64 : 32),
+                                (int32_t)row0);
+                }
+            }
+            for (int64_t j = (it > kStagesA ? it - kStagesA : 0); j < it; ++j)
+                mbar_wait(&a_full[j % kStagesA], (uint32_t)(j / kStagesA) & 1, 2, nullptr);
+        }
+    } else if (GATHER && warp >= kWarpA0) {
+        // A producers (gather_mm): thread g copies 16-byte chunk c = g % 8 of
+        // the 128-byte K slice for rows rsub + 16 i (i < 8), rsub = g / 8, so
+        // each warp instruction moves 4 whole 128-byte row slices.  Its copies
+        // of slice `it` form one cp.async group; once a group is kGatherLag
+        // groups old it has landed, and the thread publishes it to the async
+        // proxy and arrives on the stage's barrier.
+        const int g = threadIdx.x - kWarpA0 * 32;
+        const int c = g & 7, rsub = g >> 3;
+        const uint32_t sw = (uint32_t)((c ^ (rsub & 7)) << 4);  // SWIZZLE_128B: chunk ^ (row & 7)
+        const char *a = static_cast<const char *>(args.a);
+        int64_t it = 0;
+        bool ok = true;
+        for (int64_t w = blockIdx.x; w < work && ok; w += gridDim.x) {
+            int64_t rel, row0, row_end;
+            tile_rows(args, w / args.nbn, rel, row0, row_end);
+            const char *src[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int64_t row = row0 + rsub + 16 * i;
+                src[i] = row < row_end ? a + (int64_t)args.perm[row] * args.a_row_bytes + c * 16
+                                       : nullptr;
+            }
+            for (int kb = 0; kb < kb_n; ++kb, ++it) {
+                const int s = (int)(it % kStagesA);
+                if (it >= kStagesA &&
+                    !(ok = mbar_wait(&a_empty[s], (uint32_t)((it / kStagesA) - 1) & 1, 1, abort)))
+                    break;
+                const int64_t koff = (int64_t)kb * 128;
+                const bool kin = koff + c * 16 < args.a_row_bytes;
+                const uint32_t dst = smem_u32(sa + s * kABytes) + (uint32_t)rsub * 128 + sw;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const bool live = src[i] != nullptr && kin;
+                    cp_async16(dst + (uint32_t)i * 16 * 128, live ? src[i] + koff : a,
+                               live ? 16u : 0u);
+                }
+                cp_async_commit();
+                if (it >= kGatherLag) {
+                    cp_async_wait<kGatherLag>();
+                    fence_proxy_async_smem();
+                    mbar_arrive(&a_full[(it - kGatherLag) % kStagesA]);
+                }
+            }
+        }
+        // every copy issued above has landed before the CTA moves on; stages
+        // not yet published are published (an aborted CTA skips that)
+        cp_async_wait<0>();
+        fence_proxy_async_smem();
+        if (ok)
+            for (int64_t j = (it > kGatherLag ? it - kGatherLag : 0); j < it; ++j)
+                mbar_arrive(&a_full[j % kStagesA]);
+    } else if (warp == kWarpMma) {
         if (lane == 0) {
             // MMA issuer: tile t accumulates into accumulator t & 1
             const uint32_t idesc = instr_desc(BF16, args.bn);
@@ -267,15 +378,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t dacc = tmem + (uint32_t)b * acc_cols;
                 for (int kb = 0; kb < kb_n; ++kb, ++it) {
-                    const int s = (int)(it % kStages);
-                    if (!(ok = mbar_wait(&full[s], (uint32_t)(it / kStages) & 1, 3, abort))) break;
+                    const int s_a = (int)(it % kStagesA), s_b = (int)(it % kStagesB);
+                    if (!(ok = mbar_wait(&a_full[s_a], (uint32_t)(it / kStagesA) & 1, 3, abort))) break;
+                    if (!(ok = mbar_wait(&b_full[s_b], (uint32_t)(it / kStagesB) & 1, 3, abort))) break;
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    const uint64_t ad = smem_desc(smem_u32(sa + s * a_bytes));
-                    const uint64_t bd = smem_desc(smem_u32(sb + s * b_bytes));
+                    const uint64_t ad = smem_desc(smem_u32(sa + s_a * kABytes));
+                    const uint64_t bd = smem_desc(smem_u32(sb + s_b * b_bytes));
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)  // 4 MMAs of 32 bytes of K per 128-byte slice
                         mma<BF16>(dacc, ad + kk * 2, bd + kk * 2, idesc, (kb | kk) != 0);
-                    mma_commit(&empty[s]);
+                    mma_commit(&a_empty[s_a]);
+                    mma_commit(&b_empty[s_b]);
                 }
                 if (ok) mma_commit(&acc_full[b]);
             }
@@ -283,7 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_commit(mma_done);
             mbar_wait(mma_done, 0, 6, nullptr);
         }
-    } else {
+    } else if (warp >= kWarpEpi0 && warp < kWarpEpi0 + 4) {
         // epilogue: warp w reads TMEM lanes [32 (w % 4), 32 (w % 4) + 32)
         const int q = warp & 3;
         int64_t t = 0;
@@ -355,7 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
-    if (warp == 1) {
+    if (warp == kWarpMma) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                      "r"(2 * acc_cols));
@@ -379,24 +492,6 @@ __global__ void k_transpose_b(const T *__restrict__ b, T *__restrict__ bt, int64
     for (int i = threadIdx.y; i < 32; i += blockDim.y) {
         int32_t n = n0 + i, k = k0 + threadIdx.x;
         if (k < d1 && n < d2) dst[(int64_t)n * d1 + k] = tile[threadIdx.x][i];
-    }
-}
-
-// sorted[i] = a[perm[i]] (gather_mm's rows grouped by relation).
-template <typename T>
-__global__ void k_gather_rows(const T *__restrict__ a, const int32_t *__restrict__ perm,
-                              T *__restrict__ sorted, int64_t n, int32_t d1) {
-    const int32_t vec = (d1 * (int32_t)sizeof(T)) % 16 == 0 ? 16 / (int32_t)sizeof(T) : 1;
-    const int64_t per_row = d1 / vec;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n * per_row;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t row = i / per_row, c = (i % per_row) * vec;
-        const int64_t src = perm[row];
-        if (vec > 1)
-            *reinterpret_cast<uint4 *>(sorted + row * d1 + c) =
-                *reinterpret_cast<const uint4 *>(a + src * d1 + c);
-        else
-            sorted[row * d1 + c] = a[src * d1 + c];
     }
 }
 
@@ -438,8 +533,18 @@ int make_map(CUtensorMap *map, const void *ptr, int bf16, int64_t inner, int64_t
 }
 
 size_t smem_bytes(int bn) {
-    return 1024 + kStages * (size_t(kBM) * 128 + size_t(bn) * 128) + 4 * 32 * kStageRowBytes +
-           8 * (2 * kStages + 5) + 16;
+    return 1024 + kStagesA * size_t(kABytes) + kStagesB * size_t(bn) * 128 +
+           4 * 32 * kStageRowBytes + 8 * (2 * kStagesA + 2 * kStagesB + 5) + 16;
+}
+
+template <bool BF16, bool GATHER>
+int launch_tc(dim3 grid, size_t smem, cudaStream_t s, const CUtensorMap &map_a,
+              const CUtensorMap &map_b, const TcArgs &args) {
+    BGL_CUDA(cudaFuncSetAttribute(k_gmm_tc<BF16, GATHER>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    k_gmm_tc<BF16, GATHER><<<grid, threads_for(GATHER), smem, s>>>(map_a, map_b, args);
+    BGL_LAUNCH_CHECK();
+    return BGL_OK;
 }
 
 }  // namespace
@@ -455,13 +560,6 @@ bool gmm_tensor_core_supported(int64_t d1, int64_t d2, int dtype) {
 bool gmm_tensor_core_fits(int64_t n, int64_t r, int64_t d2) {
     // TMA coordinates are 32-bit: rows of A and rows of the K-major B copy
     return n < (int64_t(1) << 31) && r * d2 < (int64_t(1) << 31);
-}
-
-size_t gmm_tc_extra_bytes(int64_t n, int64_t d1, int64_t r, int64_t d2, int dtype, bool gather) {
-    const int64_t elem = dtype == BGL_BF16 ? 2 : 4;
-    size_t b = size_t(r) * d1 * d2 * elem + 256;            // K-major B
-    if (gather) b += size_t(n) * d1 * elem + 256;             // rows grouped by relation
-    return b;
 }
 
 int gmm_tensor_core(const void *a, const void *b, void *out, const GmmLayout &l, int64_t n,
@@ -481,29 +579,24 @@ int gmm_tensor_core(const void *a, const void *b, void *out, const GmmLayout &l,
                                                               (int32_t)d1, (int32_t)d2);
         BGL_LAUNCH_CHECK();
     }
-    const void *a_rows = a;
-    if (l.perm) {  // gather_mm: group A's rows by relation first
-        int g = (int)((n * (d1 * elem / 16) + 255) / 256);
-        if (g > num_sms() * 16) g = num_sms() * 16;
-        if (g < 1) g = 1;
-        if (bf16)
-            k_gather_rows<__nv_bfloat16><<<g, 256, 0, s>>>((const __nv_bfloat16 *)a, l.perm,
-                                                           (__nv_bfloat16 *)l.tc_a, n, (int32_t)d1);
-        else
-            k_gather_rows<float><<<g, 256, 0, s>>>((const float *)a, l.perm, (float *)l.tc_a, n,
-                                                   (int32_t)d1);
-        BGL_LAUNCH_CHECK();
-        a_rows = l.tc_a;
-    }
     const int bn = d2 >= 256 ? 256 : (int)((d2 + 15) / 16 * 16);
     const uint32_t bk = bf16 ? 64 : 32;
+    const bool gather = l.perm != nullptr;
     CUtensorMap map_a, map_b;
-    int rc = make_map(&map_a, a_rows, bf16, d1, n, bk, kBM);
+    int rc = make_map(&map_b, l.tc_b, bf16, d1, r * d2, bk, (uint32_t)bn);
     if (rc) return rc;
-    rc = make_map(&map_b, l.tc_b, bf16, d1, r * d2, bk, (uint32_t)bn);
-    if (rc) return rc;
+    if (gather) {
+        map_a = map_b;  // not read: gather_mm's A rows are copied by the kernel's gather warps
+        if ((d1 * elem) % 16 != 0)
+            return fail(BGL_E_INVALID, "gather_mm: tensor-core rows must be 16-byte multiples");
+    } else {
+        rc = make_map(&map_a, a, bf16, d1, n, bk, kBM);
+        if (rc) return rc;
+    }
     TcArgs args;
     args.out = out;
+    args.a = a;
+    args.a_row_bytes = d1 * elem;
     args.seg_off = l.seg_off;
     args.tile_off = l.tile_off;
     args.perm = l.perm;
@@ -515,21 +608,15 @@ int gmm_tensor_core(const void *a, const void *b, void *out, const GmmLayout &l,
     args.kb = (int32_t)((d1 + bk - 1) / bk);
     args.nbn = (int32_t)((d2 + bn - 1) / bn);
     const size_t smem = smem_bytes(bn);
-    // persistent: one CTA per SM (its 4-stage ring and 2 x BN TMEM columns),
+    // persistent: one CTA per SM (its load rings and 2 x BN TMEM columns),
     // never more CTAs than (row tile, column tile) pairs could exist
     int64_t max_work = ((n + kBM - 1) / kBM + r) * args.nbn;
     dim3 grid((unsigned)(max_work < num_sms() ? max_work : num_sms()));
-    if (bf16) {
-        BGL_CUDA(cudaFuncSetAttribute(k_gmm_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)smem));
-        k_gmm_tc<true><<<grid, kThreads, smem, s>>>(map_a, map_b, args);
-    } else {
-        BGL_CUDA(cudaFuncSetAttribute(k_gmm_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)smem));
-        k_gmm_tc<false><<<grid, kThreads, smem, s>>>(map_a, map_b, args);
-    }
-    BGL_LAUNCH_CHECK();
-    return BGL_OK;
+    if (bf16)
+        return gather ? launch_tc<true, true>(grid, smem, s, map_a, map_b, args)
+                      : launch_tc<true, false>(grid, smem, s, map_a, map_b, args);
+    return gather ? launch_tc<false, true>(grid, smem, s, map_a, map_b, args)
+                  : launch_tc<false, false>(grid, smem, s, map_a, map_b, args);
 }
 
 }  // namespace bgl

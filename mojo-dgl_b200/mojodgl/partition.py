@@ -13,6 +13,14 @@ an accumulating gSpMM pass per slice as it arrives (OwnerPipeline does the
 same over a ring of point-to-point steps, one owner block per step).
 Outputs stay sharded by destination row.
 
+The ranks can also form a grid of R row groups x C column groups
+(``rank_grid``): a rank owns a block of rows of one column block of the
+features, aggregates its row group's destinations for its column block only,
+and exchanges owner blocks within its column group (R ranks).  Each rank then
+receives (R - 1) / R of N x D / C feature values instead of (P - 1) / P of
+N x D -- with C = P (one row group) no exchange at all -- while its gather
+rows are D / C wide.
+
 The host logic here (ranges, shard extraction, block layout) is plain numpy
 and is tested with gloo ranks on CPU; the kernels run through mojodgl.
 """
@@ -66,6 +74,30 @@ class DstShard:
     @property
     def num_edges(self):
         return int(self.u.size)
+
+
+def rank_grid(rank: int, world: int, cols: int):
+    """Ranks as R = world / cols row groups x `cols` column groups, rank =
+    row_group * cols + col_group: a rank aggregates the destination rows of
+    its row group for the feature columns of its column group.  Returns
+    (R, row_group, col_group)."""
+    if cols < 1 or world % cols:
+        raise ValueError("{} ranks do not split into {} column groups".format(world, cols))
+    return world // cols, rank // cols, rank % cols
+
+
+def column_group_ranks(world: int, cols: int):
+    """The ranks of every column group (the ranks that hold the same feature
+    columns for different destination rows, and exchange their owner blocks),
+    in column-group order."""
+    rows = world // cols
+    return [[rg * cols + cg for rg in range(rows)] for cg in range(cols)]
+
+
+def column_range(d: int, cols: int, col_group: int):
+    """Feature columns [c0, c1) of a column group: d split into `cols` near-equal
+    contiguous ranges."""
+    return d * col_group // cols, d * (col_group + 1) // cols
 
 
 def segment_balanced_ranges(seglen: np.ndarray, parts: int):
@@ -299,13 +331,15 @@ class SlicePipeline:
     the same messages slice by slice (compared with a tolerance against the
     single-GPU order)."""
 
-    def __init__(self, u, v, lo, hi, rank, world, num_nodes, slices=4):
+    def __init__(self, u, v, lo, hi, rank, world, num_nodes, slices=4, group=None):
         import torch
 
         from . import _tensor as T
         from ._lib import check, lib
 
-        self.rank, self.world = rank, world
+        # rank / world / group: this rank's place among the ranks that exchange
+        # owner blocks (all ranks, or one column group of a rank grid)
+        self.rank, self.world, self.group = rank, world, group
         self.lo, self.hi = int(lo), int(hi)
         self.blk, self.owners = owner_blocks(num_nodes, world)
         self.slices = int(slices)
@@ -351,31 +385,32 @@ class SlicePipeline:
         def on_slice(c, gathered, first, last):
             self._pass(c, gathered, out, reduce_op, first, last, arg_e, ws)
 
-        slice_exchange(my_block, self.sb, self.slices, self.world, bufs, on_slice)
+        slice_exchange(my_block, self.sb, self.slices, self.world, bufs, on_slice, self.group)
         return out
 
 
-def slice_exchange(my_block, sb, slices, world, bufs, on_slice):
+def slice_exchange(my_block, sb, slices, world, bufs, on_slice, group=None):
     """Hand on_slice(c, gathered, first, last) every slice c of all ranks'
     blocks, gathered rank-major (world * sb rows), gathering slice c + 1
     while slice c is processed; the two buffers alternate, and a buffer is
     refilled only after the work queued on it (a collective is ordered after
     the work already on the current stream).  NCCL gathers into one tensor
     asynchronously; other backends (gloo, for the CPU tests) gather a list
-    and copy it in."""
+    and copy it in.  ``group``: the process group of the ranks that exchange
+    (None: all ranks)."""
     import torch
     import torch.distributed as dist
 
     if bufs is None:
         bufs = [my_block.new_empty((world * sb,) + tuple(my_block.shape[1:])) for _ in range(2)]
-    nccl = dist.get_backend() == "nccl"
+    nccl = dist.get_backend(group) == "nccl"
 
     def issue(c):
         part = my_block[c * sb:(c + 1) * sb]
         if nccl:
-            return dist.all_gather_into_tensor(bufs[c % 2], part, async_op=True)
+            return dist.all_gather_into_tensor(bufs[c % 2], part, group=group, async_op=True)
         pieces = [torch.empty_like(part) for _ in range(world)]
-        dist.all_gather(pieces, part.contiguous())
+        dist.all_gather(pieces, part.contiguous(), group=group)
         torch.cat(pieces, out=bufs[c % 2])
         return None
 

@@ -347,3 +347,90 @@ def test_other_ops_shard_and_stitch_to_the_single_process_result(world):
     want = orc.gather_mm(ga, bm, idx)
     got = np.concatenate([t[5][2] for t in results])
     np.testing.assert_array_equal(got, want)
+
+
+def _grid_rank(rank, world, port, q, cols, slices):
+    """A rank of an R x C grid: its row group's destinations, its column
+    group's feature columns, owner blocks exchanged by sliced all-gathers
+    within the column group only."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import sys
+
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        sys.path.insert(0, root)
+        from oracle import oracle as orc
+
+        from mojodgl.partition import (column_group_ranks, column_range, rank_grid,
+                                       slice_exchange, slice_of, slice_rows)
+
+        rows, rg, cg = rank_grid(rank, world, cols)
+        groups = [dist.new_group(r) for r in column_group_ranks(world, cols)]
+        u, v, h, n = graph(seed=17)
+        c0, c1 = column_range(h.shape[1], cols, cg)
+        hc = np.ascontiguousarray(h[:, c0:c1])
+        bounds = edge_balanced_ranges(np.bincount(v, minlength=n), rows)
+        lo, hi = int(bounds[rg]), int(bounds[rg + 1])
+        blk, owners = owner_blocks(n, rows)
+        sb = slice_rows(blk, slices)
+        a, b = owners[rg]
+        mine = torch.zeros(slices * sb, c1 - c0, dtype=torch.float64)
+        mine[: b - a] = torch.from_numpy(hc[a:b])
+        sel = np.nonzero((v >= lo) & (v < hi))[0]
+        cc, local = slice_of(u[sel], blk, sb)
+        sums = np.zeros((hi - lo, c1 - c0))
+        best = np.full((hi - lo, c1 - c0), -np.inf)
+        best_e = np.full((hi - lo, c1 - c0), -1, dtype=np.int64)
+
+        def on_slice(c, gathered, first, last):
+            assert gathered.shape == (rows * sb, c1 - c0)
+            k = np.nonzero(cc == c)[0]
+            og = orc.Graph(local[k], v[sel[k]] - lo, num_nodes=max(rows * sb, hi - lo))
+            x = gathered.numpy()
+            part = orc.gspmm(og, "copy_lhs", "sum", x, None)[: hi - lo]
+            sums[:] = part if first else sums + part
+            mx, _, ae = orc.gspmm(og, "copy_lhs", "max", x, None, with_arg=True)
+            mx, ae = mx[: hi - lo], ae[: hi - lo]
+            ge = np.where(ae >= 0, sel[k][np.maximum(ae, 0)], -1)
+            take = (mx > best) | ((mx == best) & (ge >= 0) & ((best_e < 0) | (ge < best_e)))
+            best[take] = mx[take]
+            best_e[take] = ge[take]
+
+        slice_exchange(mine, sb, slices, rows, None, on_slice, groups[cg])
+        q.put((rank, lo, hi, c0, c1, sums, best, best_e))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,cols", [(2, 2), (4, 2), (4, 4)])
+def test_rank_grid_reproduces_the_single_process_result(world, cols):
+    """Row x column rank grids: the pieces (row range x column range) of all
+    ranks tile the single-process result; sums to rtol 1e-12, max and its
+    edge ids exactly."""
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_grid_rank, args=(r, world, port, q, cols, 3))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    from oracle import oracle as orc
+
+    u, v, h, n = graph(seed=17)
+    og = orc.Graph(u, v, num_nodes=n)
+    want_sum = orc.gspmm(og, "copy_lhs", "sum", h, None)
+    want_max, _, want_e = orc.gspmm(og, "copy_lhs", "max", h, None, with_arg=True)
+    covered = np.zeros(want_sum.shape, dtype=np.int64)
+    for rank, lo, hi, c0, c1, sums, best, best_e in results:
+        np.testing.assert_allclose(sums, want_sum[lo:hi, c0:c1], rtol=1e-12, atol=1e-12)
+        np.testing.assert_array_equal(best, want_max[lo:hi, c0:c1])
+        np.testing.assert_array_equal(best_e, want_e[lo:hi, c0:c1])
+        covered[lo:hi, c0:c1] += 1
+    assert np.all(covered == 1)
