@@ -35,16 +35,29 @@ __device__ int g_bgl_tc_error = 0;
 
 namespace {
 
+// Ring depths and epilogue width (build-time tuning knobs; shared memory:
+// stagesA x 16 KB + stagesB x BN x 128 B + epilogue warps x 4 KB <= 227 KB).
+#ifndef BGL_GMM_STAGES_A
+#define BGL_GMM_STAGES_A 6
+#endif
+#ifndef BGL_GMM_STAGES_B
+#define BGL_GMM_STAGES_B 3
+#endif
+#ifndef BGL_GMM_EPI_WARPS
+#define BGL_GMM_EPI_WARPS 4
+#endif
 constexpr int kBM = 128;
-constexpr int kStagesA = 6;  // A slices in flight (DRAM latency)
-constexpr int kStagesB = 3;  // B slices in flight (L2 latency)
+constexpr int kStagesA = BGL_GMM_STAGES_A;  // A slices in flight (DRAM latency)
+constexpr int kStagesB = BGL_GMM_STAGES_B;  // B slices in flight (L2 latency)
+constexpr int kEpiWarps = BGL_GMM_EPI_WARPS;  // 4 or 8: one or two warps per TMEM lane quarter
+static_assert(kEpiWarps == 4 || kEpiWarps == 8, "epilogue warps: 4 or 8");
 constexpr int kGatherLag = kStagesA - 2;  // cp.async groups a gather thread keeps open
 constexpr int kStageRowBytes = 128;  // epilogue staging: 32 fp32 (or bf16 pairs) per row
 constexpr int kABytes = kBM * 128;   // one A slice: 128 rows x 128 bytes
 constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
 
 // Warp roles.
-constexpr int kWarpB = 0, kWarpMma = 1, kWarpEpi0 = 2, kWarpA0 = 6;
+constexpr int kWarpB = 0, kWarpMma = 1, kWarpEpi0 = 2, kWarpA0 = kWarpEpi0 + kEpiWarps;
 __host__ __device__ constexpr int threads_for(bool gather) { return 32 * (kWarpA0 + (gather ? 4 : 1)); }
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -228,7 +241,8 @@ __global__ void __launch_bounds__(threads_for(GATHER), 1)
     unsigned char *sb = sa + kStagesA * kABytes;
     // epilogue staging: per epilogue warp 32 rows x 128 bytes
     uint4 *staging = reinterpret_cast<uint4 *>(sb + kStagesB * b_bytes);
-    uint64_t *a_full = reinterpret_cast<uint64_t *>(sb + kStagesB * b_bytes + 4 * kStageRowBytes * 32);
+    uint64_t *a_full =
+        reinterpret_cast<uint64_t *>(sb + kStagesB * b_bytes + kEpiWarps * kStageRowBytes * 32);
     uint64_t *a_empty = a_full + kStagesA;
     uint64_t *b_full = a_empty + kStagesA;
     uint64_t *b_empty = b_full + kStagesB;
@@ -250,7 +264,7 @@ __global__ void __launch_bounds__(threads_for(GATHER), 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], 4);  // one arrive per epilogue warp
+            mbar_init(&acc_empty[b], kEpiWarps);  // one arrive per epilogue warp
         }
         mbar_init(mma_done, 1);
         *abort = 0;
@@ -396,9 +410,12 @@ __global__ void __launch_bounds__(threads_for(GATHER), 1)
             mma_commit(mma_done);
             mbar_wait(mma_done, 0, 6, nullptr);
         }
-    } else if (warp >= kWarpEpi0 && warp < kWarpEpi0 + 4) {
-        // epilogue: warp w reads TMEM lanes [32 (w % 4), 32 (w % 4) + 32)
+    } else if (warp >= kWarpEpi0 && warp < kWarpEpi0 + kEpiWarps) {
+        // epilogue: warp w reads TMEM lanes [32 (w % 4), 32 (w % 4) + 32); with
+        // 8 epilogue warps the two warps of a lane quarter take alternate
+        // 32-column chunks
         const int q = warp & 3;
+        const int part = (warp - kWarpEpi0) >> 2, parts = kEpiWarps >> 2;
         int64_t t = 0;
         for (int64_t w = blockIdx.x; w < work; w += gridDim.x, ++t) {
             const int b = (int)(t & 1);
@@ -417,8 +434,8 @@ __global__ void __launch_bounds__(threads_for(GATHER), 1)
             // 128-byte (64-byte bf16) row segments, 4 (8) rows per instruction
             constexpr int CPR = BF16 ? 4 : 8;  // 16-byte chunks per staged row
             constexpr int RPP = 32 / CPR;       // rows per store instruction
-            uint4 *stg = staging + q * 32 * 8;
-            for (int c = 0; c < args.bn; c += 32) {
+            uint4 *stg = staging + (warp - kWarpEpi0) * 32 * 8;
+            for (int c = 32 * part; c < args.bn; c += 32 * parts) {
                 uint32_t v[32];
                 tmem_ld16(taddr + (uint32_t)c, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
                 tmem_ld16(taddr + (uint32_t)c + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
@@ -534,7 +551,7 @@ int make_map(CUtensorMap *map, const void *ptr, int bf16, int64_t inner, int64_t
 
 size_t smem_bytes(int bn) {
     return 1024 + kStagesA * size_t(kABytes) + kStagesB * size_t(bn) * 128 +
-           4 * 32 * kStageRowBytes + 8 * (2 * kStagesA + 2 * kStagesB + 5) + 16;
+           kEpiWarps * 32 * kStageRowBytes + 8 * (2 * kStagesA + 2 * kStagesB + 5) + 16;
 }
 
 template <bool BF16, bool GATHER>
