@@ -13,9 +13,10 @@
 // issues tcgen05.mma (kind::tf32 for fp32 inputs, kind::f16 with bf16 for bf16
 // inputs) into one of two 128 x BN fp32 accumulators in tensor memory; warps
 // 2-5 read the other accumulator back with tcgen05.ld (each warp its 32-lane
-// quarter), transpose them through shared memory and store whole row segments
-// (rows scattered through `perm` for gather_mm) while the next tile's loads and
-// MMAs run.
+// quarter) into a swizzled shared-memory staging box and write it with a TMA
+// tile store (segment_mm rows inside the segment), or store the rows
+// themselves (a segment's last partial tile; gather_mm's rows, scattered
+// through `perm`), while the next tile's loads and MMAs run.
 //
 // Every mbarrier wait is bounded (kTimeoutNs of %globaltimer); the first to
 // expire records an error code in g_bgl_tc_error and raises a CTA-wide abort
@@ -51,7 +52,6 @@ constexpr int kStagesA = BGL_GMM_STAGES_A;  // A slices in flight (DRAM latency)
 constexpr int kStagesB = BGL_GMM_STAGES_B;  // B slices in flight (L2 latency)
 constexpr int kEpiWarps = BGL_GMM_EPI_WARPS;  // 4 or 8: one or two warps per TMEM lane quarter
 static_assert(kEpiWarps == 4 || kEpiWarps == 8, "epilogue warps: 4 or 8");
-constexpr int kGatherLag = kStagesA - 2;  // cp.async groups a gather thread keeps open
 constexpr int kStageRowBytes = 128;  // epilogue staging: 32 fp32 (or bf16 pairs) per row
 constexpr int kABytes = kBM * 128;   // one A slice: 128 rows x 128 bytes
 constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
@@ -143,6 +143,27 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// TMA tile store of a staged (SWIZZLE_128B) box; the bulk-group waits let the
+// staging buffer be rewritten once the store has read it.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int32_t c0,
+                                             int32_t c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(c0), "r"(c1), "r"(smem_u32(src))
+        : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 // K-major, SWIZZLE_128B shared-memory matrix descriptor: rows of 128 bytes,
 // 8-row groups 1024 bytes apart (SBO), LBO unused (1), version 1, layout 2.
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
@@ -229,22 +250,26 @@ __device__ __forceinline__ void tile_rows(const TcArgs &args, int64_t tile, int6
 template <bool BF16, bool GATHER>
 __global__ void __launch_bounds__(threads_for(GATHER), 1)
     k_gmm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-             const TcArgs args) {
+             const __grid_constant__ CUtensorMap map_out, const TcArgs args) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
+    constexpr int SA = kStagesA;
+    constexpr int kLag = SA - 2;  // cp.async groups a gather thread keeps open
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t row_tiles = args.tile_off[args.r];
-    const int64_t work = row_tiles * args.nbn;  // (row tile, column tile) pairs
-    const uint32_t b_bytes = (uint32_t)args.bn * 128;
+    // this CTA's (row tile, column tile) pairs w = row_tile * nbn + column_tile:
+    // blockIdx.x, blockIdx.x + gridDim.x, ... below the pair count
+    const int64_t work = args.tile_off[args.r] * args.nbn;
+    const uint32_t b_bytes = (uint32_t)args.bn * 128;  // one B slice
+    const uint32_t b_region = kStagesB * b_bytes;
     // stage buffers, each 1024-byte aligned (the SWIZZLE_128B atom)
     uintptr_t base = (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023);
     unsigned char *sa = reinterpret_cast<unsigned char *>(base);
-    unsigned char *sb = sa + kStagesA * kABytes;
-    // epilogue staging: per epilogue warp 32 rows x 128 bytes
-    uint4 *staging = reinterpret_cast<uint4 *>(sb + kStagesB * b_bytes);
+    unsigned char *sb = sa + SA * kABytes;
+    // epilogue staging: per epilogue warp two buffers of 32 rows x 128 bytes
+    uint4 *staging = reinterpret_cast<uint4 *>(sb + b_region);
     uint64_t *a_full =
-        reinterpret_cast<uint64_t *>(sb + kStagesB * b_bytes + kEpiWarps * kStageRowBytes * 32);
-    uint64_t *a_empty = a_full + kStagesA;
-    uint64_t *b_full = a_empty + kStagesA;
+        reinterpret_cast<uint64_t *>(sb + b_region + kEpiWarps * 2 * kStageRowBytes * 32);
+    uint64_t *a_empty = a_full + SA;
+    uint64_t *b_full = a_empty + SA;
     uint64_t *b_empty = b_full + kStagesB;
     uint64_t *acc_full = b_empty + kStagesB;  // [2]: accumulator b holds a finished tile
     uint64_t *acc_empty = acc_full + 2;       // [2]: the epilogue has read accumulator b
@@ -253,7 +278,7 @@ __global__ void __launch_bounds__(threads_for(GATHER), 1)
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStagesA; ++s) {
+        for (int s = 0; s < SA; ++s) {
             // gather: one arrive per gather thread once its copies have landed
             mbar_init(&a_full[s], GATHER ? 128 : 1);
             mbar_init(&a_empty[s], 1);
@@ -315,24 +340,23 @@ __global__ void __launch_bounds__(threads_for(GATHER), 1)
                 int64_t rel, row0, row_end;
                 tile_rows(args, w / args.nbn, rel, row0, row_end);
                 for (int kb = 0; kb < kb_n; ++kb, ++it) {
-                    const int s = (int)(it % kStagesA);
-                    if (it >= kStagesA &&
-                        !(ok = mbar_wait(&a_empty[s], (uint32_t)((it / kStagesA) - 1) & 1, 1, abort)))
+                    const int s = (int)(it % SA);
+                    if (it >= SA && !(ok = mbar_wait(&a_empty[s], (uint32_t)((it / SA) - 1) & 1, 1, abort)))
                         break;
                     mbar_arrive_expect_tx(&a_full[s], kABytes);
                     tma_load_2d(sa + s * kABytes, &map_a, &a_full[s], kb * (BF16 ? 64 : 32),
                                 (int32_t)row0);
                 }
             }
-            for (int64_t j = (it > kStagesA ? it - kStagesA : 0); j < it; ++j)
-                mbar_wait(&a_full[j % kStagesA], (uint32_t)(j / kStagesA) & 1, 2, nullptr);
+            for (int64_t j = (it > SA ? it - SA : 0); j < it; ++j)
+                mbar_wait(&a_full[j % SA], (uint32_t)(j / SA) & 1, 2, nullptr);
         }
     } else if (GATHER && warp >= kWarpA0) {
         // A producers (gather_mm): thread g copies 16-byte chunk c = g % 8 of
         // the 128-byte K slice for rows rsub + 16 i (i < 8), rsub = g / 8, so
         // each warp instruction moves 4 whole 128-byte row slices.  Its copies
-        // of slice `it` form one cp.async group; once a group is kGatherLag
-        // groups old it has landed, and the thread publishes it to the async
+        // of slice `it` form one cp.async group; once a group is kLag (ring
+        // depth - 2) groups old it has landed, and the thread publishes it to the async
         // proxy and arrives on the stage's barrier.
         const int g = threadIdx.x - kWarpA0 * 32;
         const int c = g & 7, rsub = g >> 3;
@@ -351,9 +375,9 @@ __global__ void __launch_bounds__(threads_for(GATHER), 1)
                                        : nullptr;
             }
             for (int kb = 0; kb < kb_n; ++kb, ++it) {
-                const int s = (int)(it % kStagesA);
-                if (it >= kStagesA &&
-                    !(ok = mbar_wait(&a_empty[s], (uint32_t)((it / kStagesA) - 1) & 1, 1, abort)))
+                const int s = (int)(it % SA);
+                if (it >= SA &&
+                    !(ok = mbar_wait(&a_empty[s], (uint32_t)((it / SA) - 1) & 1, 1, abort)))
                     break;
                 const int64_t koff = (int64_t)kb * 128;
                 const bool kin = koff + c * 16 < args.a_row_bytes;
@@ -365,10 +389,10 @@ __global__ void __launch_bounds__(threads_for(GATHER), 1)
                                live ? 16u : 0u);
                 }
                 cp_async_commit();
-                if (it >= kGatherLag) {
-                    cp_async_wait<kGatherLag>();
+                if (it >= kLag) {
+                    cp_async_wait<kLag>();
                     fence_proxy_async_smem();
-                    mbar_arrive(&a_full[(it - kGatherLag) % kStagesA]);
+                    mbar_arrive(&a_full[(it - kLag) % SA]);
                 }
             }
         }
@@ -377,8 +401,8 @@ __global__ void __launch_bounds__(threads_for(GATHER), 1)
         cp_async_wait<0>();
         fence_proxy_async_smem();
         if (ok)
-            for (int64_t j = (it > kGatherLag ? it - kGatherLag : 0); j < it; ++j)
-                mbar_arrive(&a_full[j % kStagesA]);
+            for (int64_t j = (it > kLag ? it - kLag : 0); j < it; ++j)
+                mbar_arrive(&a_full[j % SA]);
     } else if (warp == kWarpMma) {
         if (lane == 0) {
             // MMA issuer: tile t accumulates into accumulator t & 1
@@ -392,8 +416,8 @@ __global__ void __launch_bounds__(threads_for(GATHER), 1)
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t dacc = tmem + (uint32_t)b * acc_cols;
                 for (int kb = 0; kb < kb_n; ++kb, ++it) {
-                    const int s_a = (int)(it % kStagesA), s_b = (int)(it % kStagesB);
-                    if (!(ok = mbar_wait(&a_full[s_a], (uint32_t)(it / kStagesA) & 1, 3, abort))) break;
+                    const int s_a = (int)(it % SA), s_b = (int)(it % kStagesB);
+                    if (!(ok = mbar_wait(&a_full[s_a], (uint32_t)(it / SA) & 1, 3, abort))) break;
                     if (!(ok = mbar_wait(&b_full[s_b], (uint32_t)(it / kStagesB) & 1, 3, abort))) break;
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     const uint64_t ad = smem_desc(smem_u32(sa + s_a * kABytes));
@@ -413,10 +437,21 @@ __global__ void __launch_bounds__(threads_for(GATHER), 1)
     } else if (warp >= kWarpEpi0 && warp < kWarpEpi0 + kEpiWarps) {
         // epilogue: warp w reads TMEM lanes [32 (w % 4), 32 (w % 4) + 32); with
         // 8 epilogue warps the two warps of a lane quarter take alternate
-        // 32-column chunks
+        // chunks.  A chunk is CW columns, 128 bytes of each of the warp's 32
+        // rows: each thread writes its row into a staging buffer (16-byte
+        // pieces XOR-swizzled by row -- the SWIZZLE_128B layout, so neither
+        // side conflicts on banks); when all 32 rows lie inside the segment
+        // (segment_mm) one TMA store writes the 32 x CW box, otherwise the
+        // warp stores the rows itself, 4 rows of 128 bytes per instruction
+        // (scattered through perm for gather_mm).  Two staging buffers
+        // alternate; a buffer is rewritten once the store that read it is done.
         const int q = warp & 3;
         const int part = (warp - kWarpEpi0) >> 2, parts = kEpiWarps >> 2;
+        constexpr int CW = BF16 ? 64 : 32;
+        uint4 *stg_base = staging + (warp - kWarpEpi0) * 2 * 32 * 8;
         int64_t t = 0;
+        uint32_t chunk = 0;
+        int last_commit = -1;  // staging buffer of this warp's latest TMA store
         for (int64_t w = blockIdx.x; w < work; w += gridDim.x, ++t) {
             const int b = (int)(t & 1);
             if (!mbar_wait(&acc_full[b], (uint32_t)(t >> 1) & 1, 4, abort)) break;
@@ -427,61 +462,80 @@ __global__ void __launch_bounds__(threads_for(GATHER), 1)
             const int64_t row = row0 + q * 32 + lane;
             const bool live = row < row_end;
             const int64_t orow = live ? (args.perm ? (int64_t)args.perm[row] : row) : 0;
+            const bool whole = !GATHER && row0 + q * 32 + 32 <= row_end;  // warp-uniform
             const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)b * acc_cols;
-            // 32 columns at a time: each thread writes its row's 32 values into
-            // the warp's staging rows (16-byte chunks XOR-swizzled by row, so
-            // neither side conflicts on banks), then the warp stores whole
-            // 128-byte (64-byte bf16) row segments, 4 (8) rows per instruction
-            constexpr int CPR = BF16 ? 4 : 8;  // 16-byte chunks per staged row
-            constexpr int RPP = 32 / CPR;       // rows per store instruction
-            uint4 *stg = staging + (warp - kWarpEpi0) * 32 * 8;
-            for (int c = 32 * part; c < args.bn; c += 32 * parts) {
-                uint32_t v[32];
-                tmem_ld16(taddr + (uint32_t)c, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
-                tmem_ld16(taddr + (uint32_t)c + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
-                tmem_wait_ld();
+            for (int c = CW * part; c < args.bn; c += CW * parts, ++chunk) {
+                const int buf = (int)(chunk & 1);
+                uint4 *stg = stg_base + buf * 32 * 8;
+                if (lane == 0) {
+                    if (last_commit == buf) bulk_wait_read<0>();
+                    else bulk_wait_read<1>();
+                }
+                __syncwarp();
                 if (BF16) {
+                    uint32_t v[64];
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        uint32_t w[4];
+                    for (int k = 0; k < 4; ++k)
+                        tmem_ld16(taddr + (uint32_t)(c + 16 * k),
+                                  *reinterpret_cast<uint32_t(*)[16]>(&v[16 * k]));
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        uint32_t o[4];
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
                             __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(v[8 * j + 2 * i]),
                                                                      __uint_as_float(v[8 * j + 2 * i + 1]));
-                            w[i] = *reinterpret_cast<uint32_t *>(&h);
+                            o[i] = *reinterpret_cast<uint32_t *>(&h);
                         }
-                        stg[lane * 8 + (j ^ (lane & 3))] = make_uint4(w[0], w[1], w[2], w[3]);
+                        stg[lane * 8 + (j ^ (lane & 7))] = make_uint4(o[0], o[1], o[2], o[3]);
                     }
                 } else {
+                    uint32_t v[32];
+                    tmem_ld16(taddr + (uint32_t)c, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+                    tmem_ld16(taddr + (uint32_t)c + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
+                    tmem_wait_ld();
 #pragma unroll
                     for (int j = 0; j < 8; ++j)
                         stg[lane * 8 + (j ^ (lane & 7))] =
                             make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
                 }
-                __syncwarp();
-#pragma unroll
-                for (int pass = 0; pass < 32 / RPP; ++pass) {
-                    const int rr = pass * RPP + lane / CPR, j = lane % CPR;
-                    const int64_t orr = __shfl_sync(0xffffffffu, orow, rr);
-                    const bool lr = __shfl_sync(0xffffffffu, live, rr);
-                    const int32_t col = col0 + c + j * (BF16 ? 8 : 4);  // first column of the chunk
-                    const uint4 x = stg[rr * 8 + (j ^ (rr & (CPR - 1)))];
-                    if (lr && col < args.d2) {  // d2 is a multiple of 8: chunks are whole
-                        if (BF16)
-                            *reinterpret_cast<uint4 *>(static_cast<__nv_bfloat16 *>(args.out) +
-                                                       orr * args.d2 + col) = x;
-                        else
-                            *reinterpret_cast<uint4 *>(static_cast<float *>(args.out) + orr * args.d2 +
-                                                       col) = x;
+                if (whole) {
+                    fence_proxy_async_smem();  // staged rows visible to the TMA unit
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&map_out, stg, col0 + c, (int32_t)(row0 + q * 32));
+                        bulk_commit();
+                        last_commit = buf;
                     }
+                } else {
+                    __syncwarp();
+#pragma unroll
+                    for (int pass = 0; pass < 8; ++pass) {
+                        const int rr = pass * 4 + (lane >> 3), j = lane & 7;
+                        const int64_t orr = __shfl_sync(0xffffffffu, orow, rr);
+                        const bool lr = __shfl_sync(0xffffffffu, live, rr);
+                        const int32_t col = col0 + c + j * (BF16 ? 8 : 4);  // first column of the piece
+                        const uint4 x = stg[rr * 8 + (j ^ (rr & 7))];
+                        if (lr && col < args.d2) {  // d2 is a multiple of 8: pieces are whole
+                            if (BF16)
+                                *reinterpret_cast<uint4 *>(static_cast<__nv_bfloat16 *>(args.out) +
+                                                           orr * args.d2 + col) = x;
+                            else
+                                *reinterpret_cast<uint4 *>(static_cast<float *>(args.out) +
+                                                           orr * args.d2 + col) = x;
+                        }
+                    }
+                    __syncwarp();
                 }
-                __syncwarp();
             }
             // this warp is done reading accumulator b
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[b]);
         }
+        // the warp's TMA stores have completed before the CTA exits
+        if (lane == 0) bulk_wait_all();
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
@@ -551,15 +605,15 @@ int make_map(CUtensorMap *map, const void *ptr, int bf16, int64_t inner, int64_t
 
 size_t smem_bytes(int bn) {
     return 1024 + kStagesA * size_t(kABytes) + kStagesB * size_t(bn) * 128 +
-           kEpiWarps * 32 * kStageRowBytes + 8 * (2 * kStagesA + 2 * kStagesB + 5) + 16;
+           kEpiWarps * 2 * 32 * kStageRowBytes + 8 * (2 * kStagesA + 2 * kStagesB + 5) + 16;
 }
 
 template <bool BF16, bool GATHER>
 int launch_tc(dim3 grid, size_t smem, cudaStream_t s, const CUtensorMap &map_a,
-              const CUtensorMap &map_b, const TcArgs &args) {
+              const CUtensorMap &map_b, const CUtensorMap &map_out, const TcArgs &args) {
     BGL_CUDA(cudaFuncSetAttribute(k_gmm_tc<BF16, GATHER>,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    k_gmm_tc<BF16, GATHER><<<grid, threads_for(GATHER), smem, s>>>(map_a, map_b, args);
+    k_gmm_tc<BF16, GATHER><<<grid, threads_for(GATHER), smem, s>>>(map_a, map_b, map_out, args);
     BGL_LAUNCH_CHECK();
     return BGL_OK;
 }
@@ -596,18 +650,26 @@ int gmm_tensor_core(const void *a, const void *b, void *out, const GmmLayout &l,
                                                               (int32_t)d1, (int32_t)d2);
         BGL_LAUNCH_CHECK();
     }
-    const int bn = d2 >= 256 ? 256 : (int)((d2 + 15) / 16 * 16);
     const uint32_t bk = bf16 ? 64 : 32;
+    const int64_t kb = (d1 + bk - 1) / bk;
+    const int bn = d2 >= 256 ? 256 : (int)((d2 + 15) / 16 * 16);
     const bool gather = l.perm != nullptr;
     CUtensorMap map_a, map_b;
     int rc = make_map(&map_b, l.tc_b, bf16, d1, r * d2, bk, (uint32_t)bn);
     if (rc) return rc;
+    CUtensorMap map_out;
     if (gather) {
-        map_a = map_b;  // not read: gather_mm's A rows are copied by the kernel's gather warps
+        // not read: gather_mm's A rows are copied by the kernel's gather warps
+        // and its output rows are scattered by the epilogue's own stores
+        map_a = map_b;
+        map_out = map_b;
         if ((d1 * elem) % 16 != 0)
             return fail(BGL_E_INVALID, "gather_mm: tensor-core rows must be 16-byte multiples");
     } else {
         rc = make_map(&map_a, a, bf16, d1, n, bk, kBM);
+        if (rc) return rc;
+        // epilogue boxes: 32 rows x 128 bytes (32 fp32 or 64 bf16 columns)
+        rc = make_map(&map_out, out, bf16, d2, n, bf16 ? 64 : 32, 32);
         if (rc) return rc;
     }
     TcArgs args;
@@ -622,7 +684,7 @@ int gmm_tensor_core(const void *a, const void *b, void *out, const GmmLayout &l,
     args.d1 = (int32_t)d1;
     args.d2 = (int32_t)d2;
     args.bn = bn;
-    args.kb = (int32_t)((d1 + bk - 1) / bk);
+    args.kb = (int32_t)kb;
     args.nbn = (int32_t)((d2 + bn - 1) / bn);
     const size_t smem = smem_bytes(bn);
     // persistent: one CTA per SM (its load rings and 2 x BN TMEM columns),
@@ -630,10 +692,10 @@ int gmm_tensor_core(const void *a, const void *b, void *out, const GmmLayout &l,
     int64_t max_work = ((n + kBM - 1) / kBM + r) * args.nbn;
     dim3 grid((unsigned)(max_work < num_sms() ? max_work : num_sms()));
     if (bf16)
-        return gather ? launch_tc<true, true>(grid, smem, s, map_a, map_b, args)
-                      : launch_tc<true, false>(grid, smem, s, map_a, map_b, args);
-    return gather ? launch_tc<false, true>(grid, smem, s, map_a, map_b, args)
-                  : launch_tc<false, false>(grid, smem, s, map_a, map_b, args);
+        return gather ? launch_tc<true, true>(grid, smem, s, map_a, map_b, map_out, args)
+                      : launch_tc<true, false>(grid, smem, s, map_a, map_b, map_out, args);
+    return gather ? launch_tc<false, true>(grid, smem, s, map_a, map_b, map_out, args)
+                  : launch_tc<false, false>(grid, smem, s, map_a, map_b, map_out, args);
 }
 
 }  // namespace bgl
