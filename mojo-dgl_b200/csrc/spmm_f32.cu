@@ -64,6 +64,19 @@ int by_modes(const SpmmArgs<T> &a, int red, cudaStream_t s) {
     return by_reduce<T, OP, V, J>(a, red, s);
 }
 
+// A copy op on vectors reading full rows (the common case: node or edge
+// features with no broadcast): the kernels with the read operand's mode
+// fixed, so the per-edge copy and read-back carry no mode branches (they
+// count at narrow rows, where the walk is issue-bound).
+template <typename T, int OP, int V, int J>
+int by_copy_mode(const SpmmArgs<T> &a, int red, cudaStream_t s) {
+    if constexpr (V > 1) {
+        if (OP == BGL_OP_COPY_LHS && a.lhs.full) return by_reduce<T, OP, V, J, 0, -1>(a, red, s);
+        if (OP == BGL_OP_COPY_RHS && a.rhs.full) return by_reduce<T, OP, V, J, -1, 0>(a, red, s);
+    }
+    return by_reduce<T, OP, V, J>(a, red, s);
+}
+
 }  // namespace
 
 template <typename T, int V, int J>
@@ -73,8 +86,8 @@ int launch_spmm_vj(const SpmmArgs<T> &a, int op, int red, cudaStream_t s) {
     case BGL_OP_SUB: return by_modes<T, BGL_OP_SUB, V, J>(a, red, s);
     case BGL_OP_MUL: return by_modes<T, BGL_OP_MUL, V, J>(a, red, s);
     case BGL_OP_DIV: return by_modes<T, BGL_OP_DIV, V, J>(a, red, s);
-    case BGL_OP_COPY_LHS: return by_reduce<T, BGL_OP_COPY_LHS, V, J>(a, red, s);
-    case BGL_OP_COPY_RHS: return by_reduce<T, BGL_OP_COPY_RHS, V, J>(a, red, s);
+    case BGL_OP_COPY_LHS: return by_copy_mode<T, BGL_OP_COPY_LHS, V, J>(a, red, s);
+    case BGL_OP_COPY_RHS: return by_copy_mode<T, BGL_OP_COPY_RHS, V, J>(a, red, s);
     }
     return fail(BGL_E_INVALID, "gspmm: op code %d", op);
 }
