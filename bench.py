@@ -279,13 +279,11 @@ def run_reference(args):
     return 0
 
 
-def load_traffic():
-    p = os.path.join(ROOT, "profiles", "traffic.json")
-    try:
-        with open(p) as f:
-            return json.load(f)
-    except (OSError, ValueError):
-        return {}
+# DRAM bytes (read + write) of one k_spmm copy_u mean launch over the whole
+# config-3 graph: ncu captures at 0.25 and 0.5 of the edges, reads fitted
+# linearly in the edge count and extrapolated to 125M edges, writes (the
+# N x D output) constant (profiles/gspmm_copy_u_cfg3_traffic_scales.md).
+TRAFFIC_SCALED = {"cfg3_copy_u_mean_world1": 50_570_000_000}
 
 
 def run_ours(args):
@@ -496,9 +494,11 @@ def run_ours(args):
     peak = float(peaks.get("hbm_gbs", 6650.0))
     alg = algorithmic_bytes(hi - lo, shard.shard.num_edges, dc)
     achieved = alg / (ms_kernel * 1e-3) / 1e9
-    traffic = load_traffic().get("cfg3_copy_u_mean_world{}".format(world)) if cols == 1 else None
+    traffic = (TRAFFIC_SCALED.get("cfg3_copy_u_mean_world{}".format(world))
+               if cols == 1 and args.scale == 1.0 else None)
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "traffic": traffic,
+                "traffic_source": "scaled" if traffic else None,
                 "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
                 "kernel": "bgl_gspmm copy_u mean (k_spmm_coords + k_spmm + k_spmm_fixup)",
                 "algorithmic_bytes": alg, "kernel_ms": ms_kernel}
