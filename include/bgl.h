@@ -85,7 +85,9 @@ int bgl_abi_version(void);
 /* Tuning knobs for tests and benchmarks: "spmm_min_items" (merge-path chunk
  * floor), "spmm_max_chunks" (cap on merge-path chunks; 0 = automatic),
  * "spmm_split_min" (rows with at most this many edges are never split across
- * chunks; default 512).
+ * chunks; default 512), "softmax_segment_warp" (bgl_edge_softmax with eid =
+ * NULL, i.e. segment_softmax: 1 = one warp per segment, each segment read
+ * once from DRAM, 0 = the merge-path passes; default 1).
  * Returns BGL_OK or BGL_E_INVALID for an unknown name. */
 int bgl_set_param(const char *name, int64_t value);
 

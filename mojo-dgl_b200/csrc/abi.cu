@@ -62,6 +62,10 @@ int bgl_set_param(const char *name, int64_t value) {
         bgl::params().spmm_split_min = value;
         return BGL_OK;
     }
+    if (std::strcmp(name, "softmax_segment_warp") == 0) {
+        bgl::params().softmax_segment_warp = value != 0;
+        return BGL_OK;
+    }
     return bgl::fail(BGL_E_INVALID, "bgl_set_param: unknown parameter '%s'", name);
 }
 

@@ -36,6 +36,7 @@ struct Params {
     int64_t spmm_min_items = 32;   // merge-path chunk floor (items = rows + edges)
     int64_t spmm_max_chunks = 0;   // cap on chunks, 0 = automatic
     int64_t spmm_split_min = 512;  // rows with at most this many edges are never split
+    int64_t softmax_segment_warp = 1;  // segment_softmax: one warp per segment
 };
 Params &params();
 

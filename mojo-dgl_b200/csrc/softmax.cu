@@ -59,6 +59,8 @@ struct SoftArgs {
     const int32_t *edge_row;               // optional: the row of every edge, by edge id
     int64_t rstride;                       // row_m / row_r elements between rows (2 d:
                                            // a row's maxima and reciprocals side by side)
+    const int *gate;                       // optional: run only if *gate != 0 (the
+                                           // fallback of the segment-per-warp pass)
 };
 
 // (m, s) <- the softmax statistics of the items of (m, s) followed by those of
@@ -88,6 +90,7 @@ __device__ __forceinline__ void put2(T *pa, T *pb, int64_t off, const T (&va)[V]
 // (max, sum) pieces for the others, and every item's row.
 template <typename T, int V, int CV>
 __global__ void __launch_bounds__(kSoftBlock) k_softmax_stats(const SoftArgs<T> a) {
+    if (a.gate && *a.gate == 0) return;
     constexpr int W = 32 / CV;  // items per step
     constexpr int P = BGL_SOFTMAX_DEPTH, R = P + 1;
     constexpr int SLOT = V * (int)sizeof(T);
@@ -416,6 +419,7 @@ __device__ __forceinline__ void walk_items(const SoftArgs<T> &a, int32_t y0, int
 // (max, sum) pieces of the others.
 template <typename T, int V>
 __global__ void __launch_bounds__(kSoftBlock, 3) k_softmax_walk_stats(const SoftArgs<T> a, int ts) {
+    if (a.gate && *a.gate == 0) return;
     const int t = threadIdx.x & (ts - 1);
     const int64_t chunk = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) / ts;
     if (chunk >= a.num_chunks) return;
@@ -484,6 +488,7 @@ __global__ void __launch_bounds__(kSoftBlock, 3) k_softmax_walk_stats(const Soft
 // row's statistics are loaded when the walk enters it, the next row's ahead.
 template <typename T, int V>
 __global__ void __launch_bounds__(kSoftBlock, 3) k_softmax_walk_apply(const SoftArgs<T> a, int ts) {
+    if (a.gate && *a.gate == 0) return;
     const int t = threadIdx.x & (ts - 1);
     const int64_t chunk = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) / ts;
     if (chunk >= a.num_chunks) return;
@@ -586,6 +591,7 @@ struct LaneRing {
 
 template <typename T, int V, int L>
 __global__ void __launch_bounds__(kSoftBlock, 3) k_softmax_lane_stats(const SoftArgs<T> a) {
+    if (a.gate && *a.gate == 0) return;
     using Ring = LaneRing<T, V, L>;
     constexpr int U = Ring::U, P = Ring::P, R = Ring::R, VB = Ring::VB, RUNS = Ring::RUNS;
     constexpr int W = Ring::W, S = Ring::S, GPT = Ring::GPT;
@@ -804,6 +810,7 @@ __global__ void __launch_bounds__(kSoftBlock, 3) k_softmax_lane_stats(const Soft
 // per column -- whichever takes fewer dependent loads.
 template <typename T>
 __global__ void __launch_bounds__(kSoftBlock) k_softmax_fixup(const SoftArgs<T> a) {
+    if (a.gate && *a.gate == 0) return;
     const int lane = threadIdx.x & 31;
     const int64_t chunk = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
     if (chunk >= a.num_chunks) return;
@@ -853,6 +860,7 @@ __global__ void __launch_bounds__(kSoftBlock) k_softmax_fixup(const SoftArgs<T> 
 // lanes per item, UN items of a team in flight.
 template <typename T, int V, int CV>
 __global__ void __launch_bounds__(kSoftBlock) k_softmax_apply(const SoftArgs<T> a) {
+    if (a.gate && *a.gate == 0) return;
     constexpr int UN = 4;
     const int c = (threadIdx.x & 31) % CV;
     const int64_t team = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) / CV;
@@ -916,6 +924,7 @@ __global__ void __launch_bounds__(kSoftBlock) k_softmax_apply(const SoftArgs<T> 
 #endif
 template <typename T, int V, int CV>
 __global__ void __launch_bounds__(kSoftBlock, BGL_SOFTMAX_APPLY_MINB) k_softmax_apply_edges(const SoftArgs<T> a) {
+    if (a.gate && *a.gate == 0) return;
     constexpr int UN = 4;
     const int c = (threadIdx.x & 31) % CV;
     const int64_t team = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) / CV;
@@ -965,6 +974,122 @@ __global__ void __launch_bounds__(kSoftBlock, BGL_SOFTMAX_APPLY_MINB) k_softmax_
     }
 }
 
+// ------------------------------------------------ contiguous segments
+// segment_softmax (items are the consecutive rows of `logits`, eid the
+// identity): a warp takes whole segments.  It reads a segment's rows once for
+// the per-column (max, sum) -- one online update per value, the lanes of a
+// column joined by shuffles -- and straight after reads them again for the
+// output, so the second read is served by L2: DRAM sees every value read once
+// and written once, where the merge-path passes (statistics over all chunks,
+// then the output) read it twice.  The lanes cover RPS = 32 / CV rows at a
+// time, CV 16-byte vectors a row.  A segment longer than kSegLong rows would
+// hold its warp far longer than the others: the kernel leaves it and sets the
+// gate, and the merge-path passes (gated on it) compute every row.
+constexpr int64_t kSegLong = 4096;
+#ifndef BGL_SEG_UN
+#define BGL_SEG_UN 6  // rows a lane loads before folding them (4: 6.04 ms, 6: 5.79, 8: 6.62 on config 5)
+#endif
+#ifndef BGL_SEG_MINB
+#define BGL_SEG_MINB 2  // resident blocks per SM the register budget allows
+#endif
+
+template <typename T, int CV>
+__global__ void __launch_bounds__(kSoftBlock, BGL_SEG_MINB) k_seg_softmax(const SoftArgs<T> a,
+                                                                          int *gate) {
+    constexpr int V = 16 / (int)sizeof(T);
+    constexpr int RPS = 32 / CV;
+    constexpr int UN = BGL_SEG_UN;
+    const int lane = threadIdx.x & 31;
+    const int c = lane % CV, r0 = lane / CV;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    const int64_t d = a.d;
+    for (int64_t seg = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; seg < a.num_rows;
+         seg += nwarps) {
+        const int64_t i0 = a.indptr[seg], len = a.indptr[seg + 1] - i0;
+        if (len <= 0) continue;
+        if (len > kSegLong) {
+            if (lane == 0) *gate = 1;
+            continue;
+        }
+        const T *zin = a.logits + i0 * d + c * V;
+        T m[V], sm[V];
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+            m[v] = Arith<T>::ninf();
+            sm[v] = T(0);
+        }
+        int64_t r = r0;
+        for (; r + (UN - 1) * RPS < len; r += UN * RPS) {
+            T z[UN][V];
+#pragma unroll
+            for (int u = 0; u < UN; ++u) load_vec<T, V>(zin + (r + u * RPS) * d, z[u]);
+#pragma unroll
+            for (int u = 0; u < UN; ++u)
+#pragma unroll
+                for (int v = 0; v < V; ++v) online<T>(m[v], sm[v], z[u][v]);
+        }
+        for (; r < len; r += RPS) {
+            T z[V];
+            load_vec<T, V>(zin + r * d, z);
+#pragma unroll
+            for (int v = 0; v < V; ++v) online<T>(m[v], sm[v], z[v]);
+        }
+        // the lanes holding the same column vector (lane ^ k CV) join their pieces
+#pragma unroll
+        for (int off = CV; off < 32; off <<= 1)
+#pragma unroll
+            for (int v = 0; v < V; ++v) {
+                const T m2 = __shfl_xor_sync(kFull, m[v], off);
+                const T s2 = __shfl_xor_sync(kFull, sm[v], off);
+                combine<T>(m[v], sm[v], m2, s2);
+            }
+        T rr[V];
+#pragma unroll
+        for (int v = 0; v < V; ++v) rr[v] = Arith<T>::div(T(1), sm[v]);
+        T *zout = a.out + i0 * d + c * V;
+        r = r0;
+        for (; r + (UN - 1) * RPS < len; r += UN * RPS) {
+            T z[UN][V];
+#pragma unroll
+            for (int u = 0; u < UN; ++u) load_vec<T, V>(zin + (r + u * RPS) * d, z[u]);
+#pragma unroll
+            for (int u = 0; u < UN; ++u) {
+                T o[V];
+#pragma unroll
+                for (int v = 0; v < V; ++v)
+                    o[v] = Arith<T>::mul(Arith<T>::ex(Arith<T>::sub(z[u][v], m[v])), rr[v]);
+                store_stream<T, V>(zout + (r + u * RPS) * d, o);
+            }
+        }
+        for (; r < len; r += RPS) {
+            T z[V], o[V];
+            load_vec<T, V>(zin + r * d, z);
+#pragma unroll
+            for (int v = 0; v < V; ++v)
+                o[v] = Arith<T>::mul(Arith<T>::ex(Arith<T>::sub(z[v], m[v])), rr[v]);
+            store_stream<T, V>(zout + r * d, o);
+        }
+    }
+}
+
+template <typename T>
+int launch_seg(const SoftArgs<T> &a, int cv, int *gate, cudaStream_t s) {
+    int64_t blocks = (a.num_rows * 32 + kSoftBlock - 1) / kSoftBlock;
+    const int64_t cap = int64_t(num_sms()) * 8;
+    const int grid = (int)(blocks < 1 ? 1 : blocks > cap ? cap : blocks);
+    switch (cv) {
+    case 1: k_seg_softmax<T, 1><<<grid, kSoftBlock, 0, s>>>(a, gate); break;
+    case 2: k_seg_softmax<T, 2><<<grid, kSoftBlock, 0, s>>>(a, gate); break;
+    case 4: k_seg_softmax<T, 4><<<grid, kSoftBlock, 0, s>>>(a, gate); break;
+    case 8: k_seg_softmax<T, 8><<<grid, kSoftBlock, 0, s>>>(a, gate); break;
+    case 16: k_seg_softmax<T, 16><<<grid, kSoftBlock, 0, s>>>(a, gate); break;
+    case 32: k_seg_softmax<T, 32><<<grid, kSoftBlock, 0, s>>>(a, gate); break;
+    default: return fail(BGL_E_INVALID, "softmax: no segment pass for %d vectors", cv);
+    }
+    BGL_LAUNCH_CHECK();
+    return BGL_OK;
+}
+
 struct SoftPlan {
     int vmax;  // widest vector the row width allows
     int64_t num_chunks, items, split_min;
@@ -999,6 +1124,7 @@ struct SoftLayout {
     T *head_m, *head_s, *tail_m, *tail_s;
     T *row_m, *row_r;
     int32_t *item_row;
+    int *flag;  // segment-per-warp pass: set when the merge-path passes must run
     size_t bytes;
 };
 
@@ -1016,6 +1142,7 @@ SoftLayout<T> softmax_layout(void *ws, const SoftPlan &p, int64_t rows, int64_t 
     l.row_m = c.take<T>(rows * 2 * d);
     l.row_r = l.row_m + d;
     l.item_row = c.take<int32_t>(items);
+    l.flag = c.take<int>(4);
     l.bytes = c.used + 256;
     return l;
 }
@@ -1137,7 +1264,18 @@ int run_softmax(const int64_t *indptr, const int32_t *eid, const int8_t *mask, i
     SoftArgs<T> a{indptr,   eid,        mask,       (int32_t)rows, (int32_t)items,
                   (const T *)logits, (T *)out, (int32_t)d, p.num_chunks, l.coords,
                   l.head_row, l.tail_row, l.head_m, l.head_s,      l.tail_m,
-                  l.tail_s, l.row_m,    l.row_r,    l.item_row, edge_row, 2 * d};
+                  l.tail_s, l.row_m,    l.row_r,    l.item_row, edge_row, 2 * d, nullptr};
+    // segment_softmax with rows of whole 16-byte vectors: the segment-per-warp
+    // pass; the merge-path passes below then run only if it left a segment
+    const int64_t rvec = d * (int64_t)sizeof(T) / 16;
+    if (!eid && !mask && !edge_row && params().softmax_segment_warp &&
+        (d * (int64_t)sizeof(T)) % 16 == 0 && rvec <= 32 && (rvec & (rvec - 1)) == 0 &&
+        aligned(logits, 16) && aligned(out, 16)) {
+        BGL_CUDA(cudaMemsetAsync(l.flag, 0, sizeof(int), s));
+        int rc = launch_seg<T>(a, (int)rvec, l.flag, s);
+        if (rc) return rc;
+        a.gate = l.flag;
+    }
     int cg = (int)((p.num_chunks + 1 + 255) / 256);
     k_spmm_coords<<<cg, 256, 0, s>>>(indptr, rows, items, p.items, p.split_min, p.num_chunks,
                                      l.coords);

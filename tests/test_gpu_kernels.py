@@ -166,6 +166,34 @@ def test_edge_softmax_split_rows_both_paths(orc, small_chunks, dtype, heads):
         np.testing.assert_allclose(got, want, rtol=rtol, atol=1e-7 if dtype == np.float32 else 0)
 
 
+@pytest.fixture(params=[1, 0], ids=["segment-per-warp", "merge-path"])
+def seg_mode(request):
+    """segment_softmax's two schedules: one warp per segment (the default for
+    rows of whole 16-byte vectors) and the merge-path passes."""
+    _lib.set_param("softmax_segment_warp", request.param)
+    yield request.param
+    _lib.set_param("softmax_segment_warp", 1)
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+@pytest.mark.parametrize("d", [4, 8, 64, 128, 12])
+def test_segment_softmax_schedules(orc, seg_mode, dtype, d):
+    """Geometric segment lengths with empty segments, then the same with one
+    segment longer than the per-warp bound (4,096 rows: it sends the call
+    through the merge-path passes); widths whose rows are whole 16-byte
+    vectors (4 .. 128 float32 columns) and one that is not (12)."""
+    rng = np.random.default_rng(d)
+    seglen = rng.geometric(1 / 24, size=3000)
+    seglen[[5, 17, 400]] = 0
+    rtol = 2e-5 if dtype == np.float32 else 1e-12
+    atol = 1e-7 if dtype == np.float32 else 0
+    for lens in (seglen, np.concatenate([seglen[:100], [5000], seglen[100:]])):
+        v = (rng.normal(size=(int(lens.sum()), d)) * 3).astype(dtype)
+        got = ops.segment_softmax(lens, v)
+        want = orc.segment_softmax(lens, v)
+        np.testing.assert_allclose(got, want, rtol=rtol, atol=atol)
+
+
 @pytest.fixture(params=[16, 100, 1000], ids=["chunk16", "chunk100", "chunk1000"])
 def chunk_items(request):
     """Merge-path chunks of a fixed size: 16 gives the lane walk's runs (32 /
