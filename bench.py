@@ -301,8 +301,13 @@ def run_ours(args):
         torch.cuda.set_device(local)
         import datetime
 
+        # NCCL's kernels on high-priority streams: the halo's all-gathers then
+        # take SMs as the (HBM-bound) gSpMM's blocks retire instead of waiting
+        # for the whole grid
+        nccl_opts = dist.ProcessGroupNCCL.Options()
+        nccl_opts.is_high_priority_stream = not args.nccl_normal_priority
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+                                device_id=torch.device("cuda", local), pg_options=nccl_opts)
     dev = torch.device("cuda", local)
     c = dict(CFG3)
     c["num_edges"] = int(round(c["num_edges"] * args.scale))
@@ -316,7 +321,7 @@ def run_ours(args):
     grp = None
     if world > 1 and cols > 1:
         # every rank creates every column group, in the same order
-        groups = [dist.new_group(r) for r in column_group_ranks(world, cols)]
+        groups = [dist.new_group(r, pg_options=nccl_opts) for r in column_group_ranks(world, cols)]
         grp = groups[cg]
     indeg = np.bincount(v, minlength=n)
     bounds = edge_balanced_ranges(indeg, rows_n)
@@ -744,6 +749,8 @@ def main():
     ap.add_argument("--no-extra", action="store_true", help="skip the other ops of the config")
     ap.add_argument("--cols", type=int, default=0,
                     help="column groups of the N>1 rank grid (0: the default for N)")
+    ap.add_argument("--nccl-normal-priority", action="store_true",
+                    help="NCCL on normal-priority streams (default: high priority)")
     ap.add_argument("--halo-slices", type=int, default=HALO_SLICES,
                     help="row slices of each owner block in the N>1 halo")
     ap.add_argument("--suite", default="",
