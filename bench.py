@@ -53,13 +53,14 @@ sys.path.insert(0, ROOT)
 CFG3 = dict(num_nodes=2_500_000, num_edges=125_000_000, dim=128, seed=3)
 METRIC = "gSpMM Gedge-feat/s"
 UNIT = "Gedge-feat/s"
-HALO_SLICES = 4  # feature slices of the multi-GPU halo (one all-gather + one gSpMM pass each)
+HALO_SLICES = 2  # feature slices of the multi-GPU halo (one all-gather + one gSpMM pass each)
 # column groups of the rank grid by GPU count (R = N / C row groups).  Measured
-# on config 3 (8 x B200): 1 x 2 4.22 ms per step, 1 x 4 2.40 ms against 2 x 2
-# 3.26 ms, and at N = 8 the whole-graph gSpMM at D = 16 takes 1.74 ms against
-# 1.86 ms for 4 x 2 with a 2-slice halo: the all-gather barely overlaps the
-# gSpMM, whose grid holds every SM while NCCL's kernels wait for one.
-GRID_COLS = {2: 2, 4: 4, 8: 8}
+# on config 3 (8 x B200, NCCL on high-priority streams): N = 2: 1 x 2 4.22 ms
+# per step; N = 4: 1 x 4 2.40 ms against 2 x 2 3.26 ms; N = 8: 2 x 4 with a
+# 2-slice halo 1.55 ms, 1 x 8 1.60 ms, 4 x 2 1.73 ms -- the halo's all-gather
+# barely overlaps the gSpMM, whose grid holds every SM, so the grids with
+# little or no exchange win.
+GRID_COLS = {2: 2, 4: 4, 8: 4}
 
 
 # ----------------------------------------------------------------- workload
