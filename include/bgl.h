@@ -28,8 +28,8 @@
  *     pointers non-decreasing from 0 to num_edges.  The kernels read device
  *     arrays and do not check ids against sizes they are not given; an id out
  *     of range reads outside the operand.  The Python layer (mojodgl) checks
- *     node ids when a graph is built, and bgl_csr_build only produces ids in
- *     range.
+ *     node ids when a graph is built, bgl_csr_build only produces ids in
+ *     range, and bgl_check_csr checks a CSR from elsewhere on the device.
  *
  * Op, reduce and target codes are the reference's (src/ported.mojo:44-65,
  * python/mojodgl/_lib.py:66-73).
@@ -103,6 +103,17 @@ size_t bgl_csr_build_workspace_size(int64_t num_edges, int64_t num_nodes);
 int bgl_csr_build(const int64_t *key, const int64_t *other, int64_t num_edges,
                   int64_t num_nodes, int64_t *indptr, int64_t *deg, int32_t *order,
                   int32_t *indices, void *workspace, size_t workspace_bytes, void *stream);
+/* Checks a CSR against the precondition of the native layer (no counterpart
+ * in the reference, whose Python layer validates before each call): on the
+ * stream, result[0] = the number of bad row pointers (indptr[0] != 0, a
+ * decrease, indptr[num_rows] != num_edges), result[1] = the number of bad ids
+ * (indices outside [0, num_src), eid outside [0, num_eid); either array may be
+ * NULL), result[2] = the smallest CSR position holding a bad id, -1 if none.
+ * `result` is a DEVICE int64[3]; read it after the stream reaches this call.
+ * Only the given arrays are read, within the sizes given. */
+int bgl_check_csr(const int64_t *indptr, const int32_t *indices, const int32_t *eid,
+                  int64_t num_rows, int64_t num_edges, int64_t num_src, int64_t num_eid,
+                  int64_t *result, void *stream);
 /* int64 -> int32 narrowing copy (edge endpoint arrays for gsddmm). */
 int bgl_narrow_i64(const int64_t *src, int32_t *dst, int64_t n, void *stream);
 

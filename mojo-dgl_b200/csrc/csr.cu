@@ -94,6 +94,47 @@ size_t sort_temp_bytes(int64_t ne, int64_t nn) {
     return bytes;
 }
 
+// bgl_check_csr: result[0] counts bad row pointers (indptr[0] != 0, a
+// decrease, indptr[num_rows] != num_edges), result[1] bad ids (a neighbour id
+// outside [0, num_src) or an edge id outside [0, num_eid)), result[2] the
+// smallest CSR position holding a bad id (-1 if none).  Every read is inside
+// the arrays whose sizes the caller gives; an id is only compared, never
+// followed.
+constexpr unsigned long long kNoPosition = ~0ull;  // reads -1 as int64
+
+__global__ void k_check_init(unsigned long long *r) {
+    r[0] = 0;
+    r[1] = 0;
+    r[2] = kNoPosition;
+}
+
+__global__ void k_check_csr(const int64_t *__restrict__ indptr, const int32_t *__restrict__ indices,
+                            const int32_t *__restrict__ eid, int64_t rows, int64_t ne,
+                            int64_t num_src, int64_t num_eid, unsigned long long *r) {
+    const int64_t n = rows + 1 > ne ? rows + 1 : ne;
+    unsigned long long bad_ptr = 0, bad_id = 0, first = kNoPosition;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        if (i <= rows) {
+            const int64_t p = indptr[i];
+            const bool ok = i == 0 ? p == 0 : p >= indptr[i - 1];
+            if (!ok || (i == rows && p != ne)) ++bad_ptr;
+        }
+        if (i < ne) {
+            bool ok = true;
+            if (indices) ok = ok && indices[i] >= 0 && indices[i] < num_src;
+            if (eid) ok = ok && eid[i] >= 0 && eid[i] < num_eid;
+            if (!ok) {
+                ++bad_id;
+                if ((unsigned long long)i < first) first = (unsigned long long)i;
+            }
+        }
+    }
+    if (bad_ptr) atomicAdd(&r[0], bad_ptr);
+    if (bad_id) atomicAdd(&r[1], bad_id);
+    if (first != kNoPosition) atomicMin(&r[2], first);
+}
+
 }  // namespace
 }  // namespace bgl
 
@@ -145,6 +186,25 @@ int bgl_csr_build(const int64_t *key, const int64_t *other, int64_t num_edges, i
         k_gather_other<<<grid_for(num_edges), 256, 0, s>>>(other, order, indices, num_edges);
         BGL_LAUNCH_CHECK();
     }
+    return BGL_OK;
+}
+
+int bgl_check_csr(const int64_t *indptr, const int32_t *indices, const int32_t *eid,
+                  int64_t num_rows, int64_t num_edges, int64_t num_src, int64_t num_eid,
+                  int64_t *result, void *stream) {
+    if (num_rows < 0 || num_edges < 0 || num_src < 0 || num_eid < 0)
+        return fail(BGL_E_INVALID, "bgl_check_csr: negative size");
+    if (!indptr || !result) return fail(BGL_E_INVALID, "bgl_check_csr: null indptr or result");
+    cudaStream_t s = as_stream(stream);
+    auto *r = reinterpret_cast<unsigned long long *>(result);
+    k_check_init<<<1, 1, 0, s>>>(r);
+    BGL_LAUNCH_CHECK();
+    const int64_t n = num_rows + 1 > num_edges ? num_rows + 1 : num_edges;
+    int64_t g = (n + 255) / 256;
+    const int64_t cap = int64_t(num_sms()) * 16;
+    k_check_csr<<<(int)(g < 1 ? 1 : g > cap ? cap : g), 256, 0, s>>>(
+        indptr, indices, eid, num_rows, num_edges, num_src, num_eid, r);
+    BGL_LAUNCH_CHECK();
     return BGL_OK;
 }
 

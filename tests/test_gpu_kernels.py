@@ -508,3 +508,35 @@ def test_accumulate_passes_match_one_pass(orc, red):
     else:
         np.testing.assert_allclose(out.cpu().numpy(), orc.gspmm(og, "copy_lhs", red, x, None),
                                    rtol=1e-12, atol=1e-12)
+
+
+def test_check_csr_counts_bad_row_pointers_and_ids():
+    """bgl_check_csr on a valid CSR reports nothing; with planted faults (a
+    neighbour id past the source count, a negative edge id, a decreasing row
+    pointer and a wrong last pointer) it counts each and names the first bad
+    position.  Only the validator reads the faulty arrays."""
+    lib = _lib.lib()
+    rng = np.random.default_rng(91)
+    n, ne, nsrc = 500, 8000, 700
+    v = np.sort(rng.integers(0, n, ne))
+    indptr = np.zeros(n + 1, dtype=np.int64)
+    np.cumsum(np.bincount(v, minlength=n), out=indptr[1:])
+    indices = rng.integers(0, nsrc, ne).astype(np.int32)
+    eid = rng.permutation(ne).astype(np.int32)
+    res = torch.zeros(3, dtype=torch.int64, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def check(ip, ind, ed):
+        t = [torch.from_numpy(x).cuda() for x in (ip, ind, ed)]
+        rc = lib.bgl_check_csr(t[0].data_ptr(), t[1].data_ptr(), t[2].data_ptr(), n, ne, nsrc,
+                               ne, res.data_ptr(), stream)
+        assert rc == 0, lib.bgl_last_error()
+        return res.cpu().tolist()
+
+    assert check(indptr, indices, eid) == [0, 0, -1]
+    bad_ind, bad_eid, bad_ptr = indices.copy(), eid.copy(), indptr.copy()
+    bad_ind[4321] = nsrc + 5
+    bad_eid[777] = -3
+    bad_ptr[100] = bad_ptr[101] + 1  # indptr[100] > indptr[101]
+    bad_ptr[n] = ne + 1
+    assert check(bad_ptr, bad_ind, bad_eid) == [2, 2, 777]
