@@ -25,12 +25,20 @@ struct SddmmArgs {
     int64_t dout;
     int64_t red_len;
     int ts;
+    bool ids_once;  // endpoint ids loaded evict-first (teams of <= 8 lanes)
 };
 
+// With narrow rows a warp covers many edges (teams of <= 8 lanes), so an
+// endpoint-id line is read by one or two warps and never again: those ids
+// are loaded evict-first (ld.global.cs) and L2 keeps the node rows the edges
+// gather (config 2's u_add_v, 32 MB tables: 0.51 -> 0.39 ms).  With wide rows
+// (a warp per edge) 32 consecutive warps share each id line, and evict-first
+// lines did not survive the row traffic between them (config 5's u_dot_v
+// 15.7 -> 16.8 ms), so those ids keep the default policy.
 __device__ __forceinline__ int64_t target_row(int tgt, const int32_t *u, const int32_t *v,
-                                              int64_t e) {
-    if (tgt == BGL_SRC) return __ldg(u + e);
-    if (tgt == BGL_DST) return __ldg(v + e);
+                                              int64_t e, bool ids_once) {
+    if (tgt == BGL_SRC) return ids_once ? __ldcs(u + e) : __ldg(u + e);
+    if (tgt == BGL_DST) return ids_once ? __ldcs(v + e) : __ldg(v + e);
     return e;
 }
 
@@ -67,8 +75,8 @@ __global__ void __launch_bounds__(256, BGL_SDDMM_MINB) k_sddmm(const SddmmArgs<T
             for (int u = 0; u < UN; ++u) {
                 const int64_t e = e0 + u * teams;
                 ok[u] = e < a.num_edges;
-                li[u] = ok[u] ? target_row(a.lt, a.u, a.v, e) : 0;
-                ri[u] = ok[u] ? target_row(a.rt, a.u, a.v, e) : 0;
+                li[u] = ok[u] ? target_row(a.lt, a.u, a.v, e, a.ids_once) : 0;
+                ri[u] = ok[u] ? target_row(a.rt, a.u, a.v, e, a.ids_once) : 0;
             }
             T acc[UN];
 #pragma unroll
@@ -116,8 +124,8 @@ __global__ void __launch_bounds__(256, BGL_SDDMM_MINB) k_sddmm(const SddmmArgs<T
                 const int64_t e = e0 + u * teams;
                 ok[u] = e < a.num_edges;
                 if (ok[u]) {
-                    if (NEED_L) li[u] = target_row(a.lt, a.u, a.v, e);
-                    if (NEED_R) ri[u] = target_row(a.rt, a.u, a.v, e);
+                    if (NEED_L) li[u] = target_row(a.lt, a.u, a.v, e, a.ids_once);
+                    if (NEED_R) ri[u] = target_row(a.rt, a.u, a.v, e, a.ids_once);
                 }
             }
             T l[UN][V], r[UN][V];
@@ -192,6 +200,7 @@ int run_sddmm(const int32_t *u, const int32_t *v, int64_t ne, const void *lhs, i
     a.dout = dout;
     a.red_len = red_len;
     a.ts = next_pow2(width / V < 1 ? 1 : width / V);
+    a.ids_once = a.ts <= 8;
     if (V == 1) return launch_sddmm<T, 1>(a, op, s);
     return launch_sddmm<T, VM>(a, op, s);
 }
