@@ -307,7 +307,8 @@ def run_ours(args):
         # for the whole grid
         nccl_opts = dist.ProcessGroupNCCL.Options()
         nccl_opts.is_high_priority_stream = not args.nccl_normal_priority
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+        pg_timeout = datetime.timedelta(seconds=120)
+        dist.init_process_group("nccl", timeout=pg_timeout,
                                 device_id=torch.device("cuda", local), pg_options=nccl_opts)
     dev = torch.device("cuda", local)
     c = dict(CFG3)
@@ -322,7 +323,8 @@ def run_ours(args):
     grp = None
     if world > 1 and cols > 1:
         # every rank creates every column group, in the same order
-        groups = [dist.new_group(r, pg_options=nccl_opts) for r in column_group_ranks(world, cols)]
+        groups = [dist.new_group(r, timeout=pg_timeout, pg_options=nccl_opts)
+                  for r in column_group_ranks(world, cols)]
         grp = groups[cg]
     indeg = np.bincount(v, minlength=n)
     bounds = edge_balanced_ranges(indeg, rows_n)
