@@ -14,16 +14,19 @@ Multi-GPU (torchrun, one rank per GPU): strong scaling of the same graph on
 an R x C rank grid (C = --cols, by default GRID_COLS[N]): a rank aggregates
 the destination rows of its row group (R ranges balanced by in-edge count)
 for the feature columns of its column group (C contiguous column blocks), and
-owns one block of rows of its column block.  A step gathers the column
-group's owner blocks slice by slice (each block cut into --halo-slices row
-slices, one NCCL all-gather per slice within the column group) and runs one
-accumulating gSpMM pass over the rank's edges whose sources fall in a slice
-as soon as it is in, while the next slice is gathered, so the halo overlaps
-the aggregation; with one row group (R = 1) a rank already holds every row of
-its columns and the step is one gSpMM.  "allgather_then_compute" times the
-unpipelined alternative (one all-gather, then the local gSpMM),
-"allgather_only" the collective alone and "compute_only" the local gSpMM
-alone.
+owns one block of rows of its column block.  With --halo peer (the default)
+a step pulls the column group's other owner blocks straight from the peers'
+memory by copy-engine copies over NVLink (CUDA IPC mappings, no SM time) and
+runs one accumulating gSpMM pass per owner block -- its own block's at once,
+each peer's as its copy lands -- so the halo overlaps the aggregation.  With
+--halo allgather the blocks are gathered slice by slice instead (each cut
+into --halo-slices row slices, one NCCL all-gather per slice within the
+column group, one pass per slice).  With one row group (R = 1) a rank
+already holds every row of its columns and the step is one gSpMM.
+"allgather_then_compute" times the unpipelined alternative (one all-gather,
+then the local gSpMM), "allgather_only" the collective alone,
+"peer_pulls_only" the copy-engine pulls alone and "compute_only" the local
+gSpMM alone.
 
 After every timed region the step's result is checked on a seeded sample of
 rows against the float64 oracle ("parity"; each rank its own rows).
@@ -293,8 +296,9 @@ def run_ours(args):
 
     import mojodgl as dgl
     from mojodgl import ops
-    from mojodgl.partition import (DeviceShard, DstShard, SlicePipeline, column_group_ranks,
-                                   column_range, edge_balanced_ranges, owner_blocks, rank_grid)
+    from mojodgl.partition import (DeviceShard, DstShard, PeerPipeline, SlicePipeline,
+                                   column_group_ranks, column_range, edge_balanced_ranges,
+                                   owner_blocks, pull_order, rank_grid)
 
     rank, world, local = dist_env()
     oracle_threads(world)  # the parity check (and at N=1 the CPU arm) run the oracle later
@@ -332,8 +336,13 @@ def run_ours(args):
     c0, c1 = column_range(d, cols, cg)
     dc = c1 - c0
     shard = DeviceShard(DstShard(u, v, lo, hi))
-    pipe = (SlicePipeline(u, v, lo, hi, rg, rows_n, n, slices=args.halo_slices, group=grp)
-            if rows_n > 1 else None)
+    peer = rows_n > 1 and args.halo == "peer"
+    if rows_n == 1:
+        pipe = None
+    elif peer:
+        pipe = PeerPipeline(u, v, lo, hi, rg, rows_n, n, dc, group=grp)
+    else:
+        pipe = SlicePipeline(u, v, lo, hi, rg, rows_n, n, slices=args.halo_slices, group=grp)
     blk, owners = owner_blocks(n, rows_n)
     own_lo, own_hi = owners[rg]
     hc = np.ascontiguousarray(h[:, c0:c1]) if cols > 1 else h
@@ -342,22 +351,27 @@ def run_ours(args):
     h_dev = torch.from_numpy(hc).to(dev)
     gathered = torch.empty((blk * rows_n, dc), dtype=torch.float32, device=dev)
     # this rank's owner block, padded to whole slices for the sliced gather
-    my_block = torch.zeros((pipe.block_rows() if pipe else blk, dc), dtype=torch.float32,
-                           device=dev)
+    my_block = torch.zeros((pipe.block_rows() if pipe and not peer else blk, dc),
+                           dtype=torch.float32, device=dev)
     my_block[: own_hi - own_lo] = h_dev[own_lo:own_hi]
+    if peer:
+        pipe.own_block().copy_(h_dev[own_lo:own_hi])
     out = torch.empty((hi - lo, dc), dtype=torch.float32, device=dev)
     ws = None
     torch.cuda.synchronize()
 
     bufs = ([torch.empty((rows_n * pipe.sb, dc), dtype=torch.float32, device=dev)
-             for _ in range(2)] if pipe else None)
+             for _ in range(2)] if pipe and not peer else None)
     pws = [None]
 
     def step():
-        # the halo overlapped with the aggregation: slice c of every owner
-        # block of the column group arrives by one all-gather while the pass
-        # over slice c - 1 runs; one row group needs no exchange
-        if pipe:
+        # the halo overlapped with the aggregation: the peers' owner blocks
+        # arrive by copy-engine pulls (or slice by slice by all-gathers) while
+        # the passes over the blocks already in run; one row group needs no
+        # exchange
+        if peer:
+            pipe.copy_u("mean", out, ws=pws)
+        elif pipe:
             pipe.copy_u(my_block, "mean", out, bufs=bufs, ws=pws)
         else:
             shard.copy_u(h_dev, "mean", out=out, workspace=ws)
@@ -393,6 +407,13 @@ def run_ours(args):
     ms_gather_only = (timed(lambda: dist.all_gather_into_tensor(gathered, my_block[:blk],
                                                                 group=grp),
                             args.steps, 1) if pipe else None)
+
+    # the copy-engine pulls alone (every peer block, on the timed stream)
+    def pulls_only():
+        for q in pull_order(rg, rows_n):
+            pipe.pull(q, torch.cuda.current_stream())
+
+    ms_pulls_only = timed(pulls_only, args.steps, 1) if peer else None
     # the gSpMM call alone (coords + main + fixup kernels) for the roofline
     feat = h_dev
     ms_kernel = timed(lambda: shard.copy_u(feat, "mean", out=out, workspace=ws), args.steps, 1)
@@ -539,16 +560,22 @@ def run_ours(args):
                        "parallelism": "single GPU" if world == 1 else
                        "{} x {} rank grid: dst-row shards x{} (balanced by in-edges) x feature-column "
                        "blocks x{}; {}".format(rows_n, cols, rows_n, cols,
+                                               "halo by copy-engine pulls of the column group's "
+                                               "owner blocks over NVLink (CUDA IPC), overlapped "
+                                               "with one gSpMM pass per block" if peer else
                                                "halo by {} sliced all-gathers per step within each "
                                                "column group, overlapped with gSpMM passes".format(
                                                    args.halo_slices) if pipe else
                                                "no exchange (each rank owns its column block)"),
-                       "grid": [rows_n, cols], "halo_slices": args.halo_slices if pipe else 0,
+                       "grid": [rows_n, cols],
+                       "halo": "peer" if peer else "allgather" if pipe else "none",
+                       "halo_slices": args.halo_slices if pipe and not peer else 0,
                        "l2": "inputs larger than L2 (h 1.28 GB, indices 0.5 GB)"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
             # per gSpMM call: coordinates, main and fixup kernels; at N > 1 one
-            # call per halo slice (the all-gathers are NCCL's kernels)
-            "gpu_launches": 3 * (args.halo_slices if pipe else 1) * args.steps,
+            # call per owner block (peer halo: copy-engine copies, no kernels;
+            # the fences are NCCL's) or per halo slice (NCCL's all-gathers)
+            "gpu_launches": 3 * (rows_n if peer else args.halo_slices if pipe else 1) * args.steps,
             "clocks": clocks.summary(), "ops": extra, "parity": parity,
             "allgather_then_compute": None if ms_allgather is None else
             {"value": e_total * d / (ms_allgather * 1e-3) / 1e9, "unit": UNIT,
@@ -558,11 +585,17 @@ def run_ours(args):
             {"ms": ms_gather_only, "bytes_received_per_rank": blk * (rows_n - 1) * dc * 4,
              "GBps_per_rank": blk * (rows_n - 1) * dc * 4 / (ms_gather_only * 1e-3) / 1e9,
              "what": "one NCCL all_gather_into_tensor of the owner blocks (the step's halo), alone"},
+            "peer_pulls_only": None if ms_pulls_only is None else
+            {"ms": ms_pulls_only, "bytes_received_per_rank": blk * (rows_n - 1) * dc * 4,
+             "GBps_per_rank": blk * (rows_n - 1) * dc * 4 / (ms_pulls_only * 1e-3) / 1e9,
+             "what": "the copy-engine pulls of the peers' owner blocks (the step's halo), alone"},
             "compute_only": {"value": e_total * d / (ms_kernel * 1e-3) / 1e9, "unit": UNIT,
                              "ms_per_step": ms_kernel,
                              "what": "local gSpMM only (features already replicated), max over ranks"},
         }
         print(json.dumps(line), flush=True)
+    if peer:
+        pipe.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -754,8 +787,11 @@ def main():
                     help="column groups of the N>1 rank grid (0: the default for N)")
     ap.add_argument("--nccl-normal-priority", action="store_true",
                     help="NCCL on normal-priority streams (default: high priority)")
+    ap.add_argument("--halo", default="peer", choices=["peer", "allgather"],
+                    help="N>1 halo exchange: copy-engine pulls from the peers' memory, or sliced "
+                         "NCCL all-gathers")
     ap.add_argument("--halo-slices", type=int, default=HALO_SLICES,
-                    help="row slices of each owner block in the N>1 halo")
+                    help="row slices of each owner block in the all-gather halo")
     ap.add_argument("--suite", default="",
                     help="time every op of the named configs (cfg2,cfg3,cfg4,cfg5 or all) instead")
     ap.add_argument("--suite-scale", type=float, default=1.0,

@@ -245,6 +245,27 @@ int bgl_gather_mm(const void *a, const void *b, const int64_t *idx_b, void *out,
  * the device and clears the word. */
 int bgl_tc_error(void);
 
+/* ------------------------------------------------ multi-GPU halo buffers */
+/* Device buffers shared between the processes of one node (one process per
+ * GPU) through CUDA IPC, and copies between them run by the copy engines:
+ * the multi-GPU gSpMM pulls its peers' feature blocks over NVLink this way,
+ * so the transfer overlaps the aggregation without taking SMs.  Not part of
+ * the reference's interface (its gSpMM runs in one process,
+ * src/ported.mojo:442-443).  Every entry point checks its byte range against
+ * the allocation that holds it and rejects a range that leaves it. */
+enum { BGL_IPC_HANDLE_BYTES = 64 };
+/* handle (BGL_IPC_HANDLE_BYTES) and offset of [ptr, ptr + bytes) within its
+ * allocation, for bgl_ipc_open in another process */
+int bgl_ipc_export(const void *ptr, int64_t bytes, void *handle, int64_t *offset);
+/* maps another process's exported allocation into the current device's
+ * context (peer access enabled on demand); *ptr = mapping + offset */
+int bgl_ipc_open(const void *handle, int64_t offset, int64_t bytes, void **ptr);
+/* unmaps what bgl_ipc_open mapped (any pointer inside the mapping) */
+int bgl_ipc_close(void *ptr);
+/* queues a copy-engine copy of `bytes` from src to dst on `stream`; either
+ * side may be a peer mapping */
+int bgl_peer_copy(void *dst, const void *src, int64_t bytes, void *stream);
+
 /* ------------------------------------------------------- array primitives */
 /* src/ported.mojo:145-190 */
 size_t bgl_cumsum_workspace_size(int64_t n);

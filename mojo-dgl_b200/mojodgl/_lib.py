@@ -45,6 +45,10 @@ SIGNATURES = {
     "bgl_csr_build": ([_P, _P, _I64, _I64, _P, _P, _P, _P, _P, _SZ, _P], _INT),
     "bgl_narrow_i64": ([_P, _P, _I64, _P], _INT),
     "bgl_check_csr": ([_P, _P, _P, _I64, _I64, _I64, _I64, _P, _P], _INT),
+    "bgl_ipc_export": ([_P, _I64, _P, _P], _INT),
+    "bgl_ipc_open": ([_P, _I64, _I64, _P], _INT),
+    "bgl_ipc_close": ([_P], _INT),
+    "bgl_peer_copy": ([_P, _P, _I64, _P], _INT),
     "bgl_gspmm_workspace_size": ([_I64, _I64, _I64, _INT, _INT], _SZ),
     "bgl_gspmm": ([_P, _P, _P, _P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64, _P, _I64, _P, _P,
                    _INT, _INT, _INT, _INT, _P, _SZ, _P], _INT),

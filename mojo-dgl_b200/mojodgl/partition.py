@@ -421,3 +421,135 @@ def slice_exchange(my_block, sb, slices, world, bufs, on_slice, group=None):
         if c + 1 < slices:
             work = issue(c + 1)
         on_slice(c, bufs[c % 2], c == 0, c == slices - 1)
+
+
+def pull_order(rank: int, world: int):
+    """The peers whose blocks rank pulls, in order: rank + 1, rank + 2, ...
+    (mod world).  At every position of the order the ranks pull from
+    distinct peers (a rotation), so each GPU serves one reader at a time."""
+    return [(rank + k) % world for k in range(1, world)]
+
+
+class PeerPipeline(OwnerPipeline):
+    """A destination-row shard whose halo arrives by copy-engine pulls
+    straight from its peers' memory, overlapped with the aggregation.
+
+    Every rank of the exchange group (all ranks, or one column group of a
+    rank grid) holds a halo buffer of world x blk rows in owner order
+    (``halo``); its own owner block (``own_block()``) is written there by the
+    caller.  The buffers are mapped into every peer's address space once,
+    through CUDA IPC.  A call then (1) meets the peers in a one-element NCCL
+    all-reduce, which completes once every rank has queued the writes of its
+    own block; (2) queues on a side stream one copy-engine copy per peer
+    block (``bgl_peer_copy``: a DMA over NVLink, no SM time), in
+    ``pull_order``; (3) runs the gSpMM pass over the edges whose sources are
+    its own rows at once, and the pass over each peer's edges once that
+    peer's copy has landed (an event), accumulating into ``out``; (4) meets
+    the peers again after its copies, and the caller's stream waits for that
+    before it returns, so no rank overwrites its block while a peer may
+    still read it.  The NCCL all-gather schedule (SlicePipeline) needs SMs
+    for its kernels while the gSpMM grid holds them all; this one does not.
+    The passes, the accumulate rules and the tie-breaking are
+    OwnerPipeline's."""
+
+    def __init__(self, u, v, lo, hi, rank, world, num_nodes, dim, dtype=None, group=None):
+        import ctypes
+
+        import torch
+        import torch.distributed as dist
+
+        from . import _tensor as T
+        from ._lib import check, lib
+
+        super().__init__(u, v, lo, hi, rank, world, num_nodes)
+        self.group = group
+        dev = T.device()
+        dtype = dtype or torch.float32
+        self.halo = torch.zeros((world * self.blk, int(dim)), dtype=dtype, device=dev)
+        self.row_bytes = int(dim) * self.halo.element_size()
+        self.copy_stream = torch.cuda.Stream(device=dev)
+        self.landed = [torch.cuda.Event() for _ in range(world)]
+        self.fence = torch.zeros(2, dtype=torch.float32, device=dev)
+        self.peer = {}
+        if world > 1:
+            nbytes = self.halo.numel() * self.halo.element_size()
+            handle = ctypes.create_string_buffer(64)
+            off = ctypes.c_int64(0)
+            check(lib().bgl_ipc_export(T.ptr(self.halo), nbytes, handle, ctypes.byref(off)),
+                  "bgl_ipc_export")
+            mine = (bytes(handle.raw), int(off.value), int(nbytes))
+            got = [None] * world
+            dist.all_gather_object(got, mine, group=group)
+            for q in range(world):
+                if q == rank:
+                    continue
+                h, o, nb = got[q]
+                if nb != nbytes:
+                    raise RuntimeError(f"PeerPipeline: rank {q} exported {nb} bytes, expected {nbytes}")
+                p = ctypes.c_void_p(0)
+                check(lib().bgl_ipc_open(h, o, nb, ctypes.byref(p)), "bgl_ipc_open")
+                self.peer[q] = int(p.value)
+            torch.cuda.synchronize()
+            dist.barrier(group=group)
+
+    def own_block(self):
+        """This rank's rows of the halo buffer: the caller writes its owner
+        block's features here (on the current stream) before a call."""
+        lo, hi = self.owners[self.rank]
+        return self.halo[self.rank * self.blk:self.rank * self.blk + (hi - lo)]
+
+    def block(self, q):
+        """Owner q's rows of the halo buffer."""
+        lo, hi = self.owners[q]
+        return self.halo[q * self.blk:q * self.blk + (hi - lo)]
+
+    def pull(self, q, stream):
+        """Queue the copy of owner q's block from its rank's halo buffer."""
+        from . import _tensor as T
+        from ._lib import check, lib
+
+        lo, hi = self.owners[q]
+        off = q * self.blk * self.row_bytes
+        nbytes = (hi - lo) * self.row_bytes
+        check(lib().bgl_peer_copy(T.ptr(self.halo) + off, self.peer[q] + off, nbytes,
+                                  stream.cuda_stream), "bgl_peer_copy")
+
+    def copy_u(self, reduce_op, out, arg_e=None, ws=None):
+        """out[rows of this shard] = reduce over in-edges of the source
+        feature, the features being every rank's own_block()."""
+        import torch
+        import torch.distributed as dist
+
+        ws = ws if ws is not None else [None]
+        order = pull_order(self.rank, self.world)
+        cur = torch.cuda.current_stream()
+        if order:
+            ready = dist.all_reduce(self.fence[:1], group=self.group, async_op=True)
+            with torch.cuda.stream(self.copy_stream):
+                ready.wait()
+                for q in order:
+                    self.pull(q, self.copy_stream)
+                    self.landed[q].record(self.copy_stream)
+                done = dist.all_reduce(self.fence[1:], group=self.group, async_op=True)
+        self._pass(self.rank, self.block(self.rank), out, reduce_op, True, not order, arg_e, ws)
+        for k, q in enumerate(order):
+            cur.wait_event(self.landed[q])
+            self._pass(q, self.block(q), out, reduce_op, False, k == len(order) - 1, arg_e, ws)
+        if order:
+            done.wait()
+        return out
+
+    def close(self):
+        """Unmap the peers' buffers (after every rank's last call)."""
+        import torch
+        import torch.distributed as dist
+
+        from ._lib import check, lib
+
+        if not self.peer:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        for q, p in self.peer.items():
+            check(lib().bgl_ipc_close(p), "bgl_ipc_close")
+        self.peer = {}

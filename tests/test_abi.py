@@ -104,6 +104,18 @@ def test_grouped_mm_validation(lib):
     assert lib.bgl_segment_mm(None, None, None, None, 1, 1, 1, 1, 7, None, 0, None) == 3
 
 
+def test_peer_buffer_validation(lib):
+    inv = 1  # BGL_E_INVALID
+    off = ctypes.c_int64(0)
+    ptr = ctypes.c_void_p(0)
+    handle = ctypes.create_string_buffer(64)
+    assert lib.bgl_peer_copy(None, None, 16, None) == inv
+    assert lib.bgl_ipc_export(None, 16, handle, ctypes.byref(off)) == inv
+    assert lib.bgl_ipc_open(None, 0, 16, ctypes.byref(ptr)) == inv
+    assert lib.bgl_ipc_open(handle, -1, 16, ctypes.byref(ptr)) == inv
+    assert lib.bgl_ipc_close(None) == inv
+
+
 @pytest.mark.skipif(__import__("torch").cuda.is_available(), reason="checks the no-GPU behaviour")
 def test_no_cpu_fallback_without_a_device():
     """Without a CUDA device every operator raises instead of computing on

@@ -43,6 +43,19 @@ def test_edge_balanced_ranges_cover_and_balance():
         assert max(per) <= v.size / parts + indeg.max()
 
 
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_pull_order_is_a_rotation(world):
+    """Every rank pulls every peer block once, and at each position of the
+    order the ranks read distinct peers."""
+    from mojodgl.partition import pull_order
+
+    orders = [pull_order(r, world) for r in range(world)]
+    for r, o in enumerate(orders):
+        assert sorted(o) == [q for q in range(world) if q != r]
+    for k in range(world - 1):
+        assert len({o[k] for o in orders}) == world
+
+
 def test_owner_blocks_tile_the_rows():
     blk, owners = owner_blocks(10, 4)
     assert blk == 3 and owners == [(0, 3), (3, 6), (6, 9), (9, 10)]
