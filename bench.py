@@ -56,14 +56,14 @@ sys.path.insert(0, ROOT)
 CFG3 = dict(num_nodes=2_500_000, num_edges=125_000_000, dim=128, seed=3)
 METRIC = "gSpMM Gedge-feat/s"
 UNIT = "Gedge-feat/s"
-HALO_SLICES = 2  # feature slices of the multi-GPU halo (one all-gather + one gSpMM pass each)
+HALO_SLICES = 2  # row slices of each owner block in the all-gather halo (--halo allgather)
 # column groups of the rank grid by GPU count (R = N / C row groups).  Measured
-# on config 3 (8 x B200, NCCL on high-priority streams): N = 2: 1 x 2 4.22 ms
-# per step; N = 4: 1 x 4 2.40 ms against 2 x 2 3.26 ms; N = 8: 2 x 4 with a
-# 2-slice halo 1.55 ms, 1 x 8 1.60 ms, 4 x 2 1.73 ms -- the halo's all-gather
-# barely overlaps the gSpMM, whose grid holds every SM, so the grids with
-# little or no exchange win.
-GRID_COLS = {2: 2, 4: 4, 8: 4}
+# on config 3 (8 x B200, copy-engine halo, ms per step): N = 2: 2 x 1 3.78
+# (1 x 2, no exchange: 4.22); N = 4: 2 x 2 2.09, 4 x 1 2.19 (1 x 4: 2.40);
+# N = 8: 2 x 4 1.28, 4 x 2 1.38, 8 x 1 1.83 (1 x 8: 1.60).  The pulls take no
+# SMs, so a grid wins while its halo (R - 1 blocks at 520-730 GB/s per rank)
+# stays under the gSpMM's time; narrower column blocks cost gSpMM efficiency.
+GRID_COLS = {2: 1, 4: 2, 8: 4}
 
 
 # ----------------------------------------------------------------- workload
