@@ -488,7 +488,9 @@ def run_ours(args):
         out_pin = torch.empty((hi - lo, dc), dtype=torch.float32).pin_memory()
 
         def e2e_step():
-            if pipe:
+            if peer:
+                pipe.own_block().copy_(h_pin, non_blocking=True)
+            elif pipe:
                 my_block[: own_hi - own_lo].copy_(h_pin, non_blocking=True)
             else:
                 h_dev.copy_(h_pin, non_blocking=True)
@@ -509,9 +511,10 @@ def run_ours(args):
         e2e = {"value": e_total * d / dt / 1e9, "unit": UNIT,
                "h2d_bytes_per_step": int(h.nbytes), "d2h_bytes_per_step": int(n * d * 4),
                "ms_per_step": dt * 1e3,
-               "path": "per rank: its pinned piece of h H2D, sliced all-gather halo within its "
-                       "column group overlapped with gSpMM passes (none with one row group), its "
-                       "output piece D2H"}
+               "path": "per rank: its pinned piece of h H2D, the halo within its column group "
+                       "({}) overlapped with gSpMM passes (none with one row group), its output "
+                       "piece D2H".format("copy-engine pulls" if peer else
+                                          "sliced all-gathers")}
 
     # -------- roofline of the dominant kernel (this rank's gSpMM)
     peaks = {}
