@@ -317,6 +317,9 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     c = dict(CFG3)
     c["num_edges"] = int(round(c["num_edges"] * args.scale))
+    if args.dim > 0:
+        c["dim"] = args.dim
+    full_size = args.scale == 1.0 and c["dim"] == CFG3["dim"]
     n, e_total, d = c["num_nodes"], c["num_edges"], c["dim"]
     u, v, h = make_cfg3(**c)
 
@@ -527,7 +530,7 @@ def run_ours(args):
     alg = algorithmic_bytes(hi - lo, shard.shard.num_edges, dc)
     achieved = alg / (ms_kernel * 1e-3) / 1e9
     traffic = (TRAFFIC_SCALED.get("cfg3_copy_u_mean_world{}".format(world))
-               if cols == 1 and args.scale == 1.0 else None)
+               if cols == 1 and full_size else None)
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "traffic": traffic,
                 "traffic_source": "scaled" if traffic else None,
@@ -556,9 +559,9 @@ def run_ours(args):
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": "cfg3 copy_u_mean (BASELINE config 3): N=2.5M, E=125M "
-                                   "lognormal out-degree, D=128 fp32" if args.scale == 1.0 else
-                                   "cfg3 copy_u_mean with edges scaled by {} (profiling case)"
-                                   .format(args.scale),
+                                   "lognormal out-degree, D=128 fp32" if full_size else
+                                   "cfg3 copy_u_mean with edges scaled by {} and D={} (profiling "
+                                   "case)".format(args.scale, d),
                        "num_nodes": n, "num_edges": e_total, "dim": d, "seed": c["seed"],
                        "parallelism": "single GPU" if world == 1 else
                        "{} x {} rank grid: dst-row shards x{} (balanced by in-edges) x feature-column "
@@ -802,6 +805,9 @@ def main():
                          "(profiling cases)")
     ap.add_argument("--scale", type=float, default=1.0,
                     help="scale the edge count (a smaller case for profiling; nodes unchanged)")
+    ap.add_argument("--dim", type=int, default=0,
+                    help="feature columns (0: the config's 128; a narrower case for profiling, "
+                         "e.g. one rank's column block)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
