@@ -248,6 +248,15 @@ __device__ __forceinline__ void store_piece(const SpmmArgs<T> &a, T *val, int32_
 #ifndef BGL_SPMM_DEPTH_BIN
 #define BGL_SPMM_DEPTH_BIN 4
 #endif
+#ifndef BGL_SPMM_MAXB
+#define BGL_SPMM_MAXB 3  // resident blocks a launch asks for at most
+#endif
+#ifndef BGL_SPMM_DEPTH_NARROW
+#define BGL_SPMM_DEPTH_NARROW 2  // the narrow ring (float copy ops, teams under a warp)
+#endif
+#ifndef BGL_SPMM_MAXB_NARROW
+#define BGL_SPMM_MAXB_NARROW 4
+#endif
 // Measured on config 3 (125M edges, 128 fp32 columns) and config 2: copy ops
 // run best with groups of 4 and 3 in flight at three blocks per SM (copy_u sum
 // 9.5 ms; groups of 2 x 6, 3 x 4, 6 x 2, or any two-block ring: 10.2-10.9 ms);
@@ -260,18 +269,22 @@ __device__ __forceinline__ void store_piece(const SpmmArgs<T> &a, T *val, int32_
 constexpr int kSpmmBlock = 256;
 constexpr int kSmemPerSm = 228 * 1024;  // shared memory per SM, 1 KB of it reserved per block
 
-template <typename T, int OP, int V>
+template <typename T, int OP, int V, bool NARROW = false>
 struct Stages {
     static constexpr bool both = OP != BGL_OP_COPY_LHS && OP != BGL_OP_COPY_RHS;
+    static_assert(!(NARROW && both), "the narrow ring is for copy ops");
     static constexpr int un = both ? BGL_SPMM_UN_BIN : BGL_SPMM_UN;
-    static constexpr int depth = both ? BGL_SPMM_DEPTH_BIN : BGL_SPMM_DEPTH;
+    static constexpr int depth = both ? BGL_SPMM_DEPTH_BIN
+                                 : NARROW ? BGL_SPMM_DEPTH_NARROW : BGL_SPMM_DEPTH;
     static constexpr int ring = depth + 1;
     static constexpr int nops = both ? 2 : 1;
     static constexpr int slot = V * (int)sizeof(T);  // bytes per lane per operand row
     static constexpr int smem = ring * un * nops * kSpmmBlock * slot;
-    // resident blocks the ring allows, at most three (85 registers a thread)
+    // resident blocks the ring allows, at most three (85 registers a
+    // thread), four for the narrow ring (64 registers)
+    static constexpr int maxb = NARROW ? BGL_SPMM_MAXB_NARROW : BGL_SPMM_MAXB;
     static constexpr int fit = kSmemPerSm / (smem + 1024);
-    static constexpr int minb = fit < 1 ? 1 : fit > 3 ? 3 : fit;
+    static constexpr int minb = fit < 1 ? 1 : fit > maxb ? maxb : fit;
     static_assert(smem <= 227 * 1024, "gather ring larger than a block's shared memory");
 };
 
@@ -284,10 +297,12 @@ struct Stages {
 // broadcast, 2 per element) when the launch knows them, -1 to read them at
 // run time.  A known mode folds every mode branch and slot stride of the
 // per-edge copy and read-back into constants.
-template <typename T, int OP, int RED, int V, int J, bool ACC, int LM = -1, int RM = -1>
-__global__ void __launch_bounds__(kSpmmBlock, (Stages<T, OP, V>::minb)) k_spmm(const SpmmArgs<T> a) {
+template <typename T, int OP, int RED, int V, int J, bool ACC, int LM = -1, int RM = -1,
+          bool NARROW = false>
+__global__ void __launch_bounds__(kSpmmBlock, (Stages<T, OP, V, NARROW>::minb))
+    k_spmm(const SpmmArgs<T> a) {
     static_assert(J == 1, "the staged gather keeps one column vector per lane");
-    using S = Stages<T, OP, V>;
+    using S = Stages<T, OP, V, NARROW>;
     constexpr int UN = S::un, P = S::depth, R = S::ring;
     constexpr bool NEED_L = OP != BGL_OP_COPY_RHS;
     constexpr bool NEED_R = OP != BGL_OP_COPY_LHS;
