@@ -113,6 +113,22 @@ __device__ __forceinline__ void fold(T &acc, int32_t &pos, T m, int32_t p) {
     }
 }
 
+// A lane's V arg indices: 16-byte stores where the address allows (V even),
+// so a warp's instruction covers whole sectors instead of one word in each.
+template <int V>
+__device__ __forceinline__ void store_i64(int64_t *p, const int64_t (&w)[V]) {
+    if constexpr (V % 2 == 0) {
+        if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+#pragma unroll
+            for (int i = 0; i < V; i += 2)
+                *reinterpret_cast<longlong2 *>(p + i) = make_longlong2(w[i], w[i + 1]);
+            return;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < V; ++i) p[i] = w[i];
+}
+
 // Writes one finished row: the mean divide, the inf->0 post-pass and the arg
 // indices are all applied here, so the row is written once.  In accumulate
 // mode the row is first folded into what `out` already holds (a partial result
@@ -149,11 +165,22 @@ __device__ __forceinline__ void emit_row(const SpmmArgs<T> &a, int64_t row, int6
             }
             store_vec<T, V>(a.out + off, o);
             if (ARG) {
+                int64_t w[V];
+                if (a.arg_u) {
 #pragma unroll
-                for (int i = 0; i < V; ++i) {
-                    int32_t p = pos[j][i];
-                    if (a.arg_u) a.arg_u[off + i] = p < 0 ? -1 : (int64_t)a.indices[p];
-                    if (a.arg_e) a.arg_e[off + i] = p < 0 ? -1 : (a.eid ? (int64_t)a.eid[p] : (int64_t)p);
+                    for (int i = 0; i < V; ++i) {
+                        const int32_t p = pos[j][i];
+                        w[i] = p < 0 ? -1 : (int64_t)a.indices[p];
+                    }
+                    store_i64<V>(a.arg_u + off, w);
+                }
+                if (a.arg_e) {
+#pragma unroll
+                    for (int i = 0; i < V; ++i) {
+                        const int32_t p = pos[j][i];
+                        w[i] = p < 0 ? -1 : (a.eid ? (int64_t)a.eid[p] : (int64_t)p);
+                    }
+                    store_i64<V>(a.arg_e + off, w);
                 }
             }
         }
