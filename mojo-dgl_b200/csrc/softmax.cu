@@ -1072,22 +1072,35 @@ __global__ void __launch_bounds__(kSoftBlock, BGL_SEG_MINB) k_seg_softmax(const 
     }
 }
 
-template <typename T>
-int launch_seg(const SoftArgs<T> &a, int cv, int *gate, cudaStream_t s) {
-    int64_t blocks = (a.num_rows * 32 + kSoftBlock - 1) / kSoftBlock;
-    const int64_t cap = int64_t(num_sms()) * 8;
+// One wave of resident blocks (the SM count times the blocks an SM holds at
+// this kernel's register count), the warps striding over the segments: a
+// fixed cap of eight blocks an SM ran 2.7 waves at three resident, the last
+// one partly empty (28.6 % of the SM's warps active in a config-5 capture).
+template <typename T, int CV>
+int launch_seg_cv(const SoftArgs<T> &a, int *gate, cudaStream_t s) {
+    auto k = k_seg_softmax<T, CV>;
+    int per_sm = 0;
+    BGL_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kSoftBlock, 0));
+    if (per_sm < 1) per_sm = 1;
+    const int64_t blocks = (a.num_rows * 32 + kSoftBlock - 1) / kSoftBlock;
+    const int64_t cap = int64_t(num_sms()) * per_sm;
     const int grid = (int)(blocks < 1 ? 1 : blocks > cap ? cap : blocks);
-    switch (cv) {
-    case 1: k_seg_softmax<T, 1><<<grid, kSoftBlock, 0, s>>>(a, gate); break;
-    case 2: k_seg_softmax<T, 2><<<grid, kSoftBlock, 0, s>>>(a, gate); break;
-    case 4: k_seg_softmax<T, 4><<<grid, kSoftBlock, 0, s>>>(a, gate); break;
-    case 8: k_seg_softmax<T, 8><<<grid, kSoftBlock, 0, s>>>(a, gate); break;
-    case 16: k_seg_softmax<T, 16><<<grid, kSoftBlock, 0, s>>>(a, gate); break;
-    case 32: k_seg_softmax<T, 32><<<grid, kSoftBlock, 0, s>>>(a, gate); break;
-    default: return fail(BGL_E_INVALID, "softmax: no segment pass for %d vectors", cv);
-    }
+    k<<<grid, kSoftBlock, 0, s>>>(a, gate);
     BGL_LAUNCH_CHECK();
     return BGL_OK;
+}
+
+template <typename T>
+int launch_seg(const SoftArgs<T> &a, int cv, int *gate, cudaStream_t s) {
+    switch (cv) {
+    case 1: return launch_seg_cv<T, 1>(a, gate, s);
+    case 2: return launch_seg_cv<T, 2>(a, gate, s);
+    case 4: return launch_seg_cv<T, 4>(a, gate, s);
+    case 8: return launch_seg_cv<T, 8>(a, gate, s);
+    case 16: return launch_seg_cv<T, 16>(a, gate, s);
+    case 32: return launch_seg_cv<T, 32>(a, gate, s);
+    }
+    return fail(BGL_E_INVALID, "softmax: no segment pass for %d vectors", cv);
 }
 
 struct SoftPlan {
